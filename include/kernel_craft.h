@@ -1,0 +1,241 @@
+/*
+ * kernel_craft.h -- C ABI of the B200 (sm_100a) quantized-linear library.
+ *
+ * Part 1 re-declares, signature for signature, the extern "C" launchers that
+ * kernel-craft's libkernels.so exports for this path; each cites the
+ * reference definition it replaces (path within the kernel-craft project).
+ * Their semantics are kept: void return, raw device pointers, the stream last,
+ * and a cudaStreamSynchronize before returning where the reference had one.
+ * Invalid arguments (which the reference never checked) launch nothing and are
+ * reported through kc_get_last_error().
+ *
+ * Part 2 is the new kc_* API: int status (KC_OK == 0), never synchronizes
+ * unless stated, never allocates device memory.  It carries the bf16 / fp16 /
+ * FP8 entry points the reference does not have (batched W4A16 GEMV, tcgen05
+ * GEMMs, bf16 collectives, sharded drivers).
+ *
+ * All pointers are device pointers unless stated; the caller owns every
+ * buffer.  Layouts are row-major.
+ */
+#ifndef KERNEL_CRAFT_H
+#define KERNEL_CRAFT_H
+
+#include <stdint.h>
+#include <stdbool.h>
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+
+#if defined(__GNUC__)
+#define KC_API __attribute__((visibility("default")))
+#else
+#define KC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ======================================================================= */
+/* Status codes                                                             */
+/* ======================================================================= */
+#define KC_OK               0
+#define KC_ERR_INVALID_ARG  1   /* a size, pointer or flag the kernel cannot take */
+#define KC_ERR_ALIGNMENT    2   /* a pointer/stride violates a documented alignment */
+#define KC_ERR_CUDA         3   /* a CUDA runtime call or launch failed */
+#define KC_ERR_NCCL         4   /* an NCCL call failed */
+#define KC_ERR_UNSUPPORTED  5   /* entry point outside this library's scope */
+#define KC_ERR_TIMEOUT      6   /* a bounded device-side wait gave up */
+
+/* Last status recorded on the calling thread by any entry point (0 = none);
+ * reading it clears it. */
+KC_API int kc_get_last_error(void);
+/* Human-readable detail for the last recorded status on this thread. */
+KC_API const char* kc_get_last_error_string(void);
+/* Library version string. */
+KC_API const char* kc_version(void);
+
+/* ======================================================================= */
+/* Part 1: reference launcher ABI (drop-in)                                 */
+/* ======================================================================= */
+
+/* src/kernels/transformer/quant_int4.cu:193.  out[r,c] = (float)(sx4(nib) - zp) * scale;
+ * packed u8[rows, cols/2] (low nibble = even col), scales f32[rows, cols/gs],
+ * zeros u8 packed two per byte, row stride floor(cols/gs/2).  Synchronizes.
+ * Requires cols even, group_size > 0 and cols % group_size == 0. */
+KC_API void launch_dequantize_int4(const uint8_t* d_packed, const float* d_scales,
+                            const uint8_t* d_zeros, float* d_output,
+                            int rows, int cols, int group_size, cudaStream_t stream);
+
+/* src/kernels/transformer/quant_int4.cu:221.  y[r] = sum_c w(r,c) * x[c] (fp32). Synchronizes. */
+KC_API void launch_gemv_int4(const uint8_t* d_packed, const float* d_scales,
+                      const uint8_t* d_zeros, const float* d_x, float* d_y,
+                      int rows, int cols, int group_size, cudaStream_t stream);
+
+/* src/kernels/transformer/fp8_quant.cu:201.  per_token: scales[r] = amax_r/448 (1 if 0),
+ * q = e4m3_satfinite(clamp(x/scale, +-448)).  Otherwise the caller's d_scales[0] is the
+ * per-tensor scale (read on the device; no host round trip).  Synchronizes. */
+KC_API void launch_quantize_fp8(const float* d_input, int8_t* d_output, float* d_scales,
+                         int rows, int cols, bool per_token, cudaStream_t stream);
+
+/* src/kernels/transformer/fp8_quant.cu:239.  x = float(e4m3) * scale[row or 0]. Synchronizes. */
+KC_API void launch_dequantize_fp8(const int8_t* d_input, const float* d_scales, float* d_output,
+                           int rows, int cols, bool per_token, cudaStream_t stream);
+
+/* src/kernels/transformer/fp8_quant.cu:265.  out[r,c] = in[r,c] / smooth[c]. Synchronizes. */
+KC_API void launch_smoothquant_scale(const float* d_input, const float* d_smooth_scales,
+                              float* d_output, int rows, int cols, cudaStream_t stream);
+
+/* src/kernels/transformer/tensor_parallel.cu:209.  y[M,N_rank] = x[M,K] * W[N_rank,K]^T (fp32). Async. */
+KC_API void launch_col_parallel_linear(const float* d_x, const float* d_W, float* d_y,
+                                int M, int N_rank, int K, cudaStream_t stream);
+
+/* src/kernels/transformer/tensor_parallel.cu:235.  out[M,N] = x_r[M,K_rank] * W[N,K_rank]^T (fp32). Async. */
+KC_API void launch_row_parallel_linear(const float* d_x_rank, const float* d_W, float* d_out,
+                                int M, int N, int K_rank, cudaStream_t stream);
+
+/* src/kernels/transformer/tensor_parallel.cu:93.  Single-GPU simulation: d_bufs is a HOST
+ * array of num_ranks device pointers; every buffer ends holding the sum (chunk c summed in
+ * rank order into rank c, then broadcast).  Synchronizes (returns at once if num_ranks <= 1). */
+KC_API void launch_ring_allreduce(float** d_bufs, int count, int num_ranks, cudaStream_t stream);
+
+/* src/kernels/transformer/tensor_parallel.cu:258.  out = [chunk_0 | ... | chunk_{R-1}]. Synchronizes. */
+KC_API void launch_allgather(float** d_chunks, float* d_output, int chunk_size, int num_ranks,
+                      cudaStream_t stream);
+
+/* src/kernels/transformer/tensor_parallel_nccl.cu:58.  ncclCommInitAll over devs. */
+KC_API void nccl_comm_init_all(void** comms, int num_comms, const int* devs);
+/* src/kernels/transformer/tensor_parallel_nccl.cu:69. */
+KC_API void nccl_comm_destroy(void* comm);
+/* src/kernels/transformer/tensor_parallel_nccl.cu:77. */
+KC_API void nccl_group_start(void);
+/* src/kernels/transformer/tensor_parallel_nccl.cu:85. */
+KC_API void nccl_group_end(void);
+/* src/kernels/transformer/tensor_parallel_nccl.cu:105.  In-place fp32 sum all-reduce. Async. */
+KC_API void launch_ring_allreduce_nccl(void* comm, float* d_buf, int count, cudaStream_t stream);
+/* src/kernels/transformer/tensor_parallel_nccl.cu:127.  fp32 all-gather, rank-major. Async. */
+KC_API void launch_allgather_nccl(void* comm, const float* d_sendbuf, float* d_recvbuf,
+                           int sendcount, cudaStream_t stream);
+/* src/kernels/transformer/tensor_parallel_nccl.cu:147.  Ranks in comm, 0 on error. */
+KC_API int nccl_comm_count(void* comm);
+/* src/kernels/transformer/tensor_parallel_nccl.cu:160.  Rank of comm, -1 on error. */
+KC_API int nccl_comm_user_rank(void* comm);
+
+/* Out-of-scope launchers that src/python/kernel_craft_torch_ops.py:105-168 resolves
+ * when it loads the library.  Exported so the unmodified bridge loads; each records
+ * KC_ERR_UNSUPPORTED and launches nothing (attention and speculative decoding are not
+ * part of this library). */
+KC_API void launch_flash_attention(const float* Q, const float* K, const float* V, float* O,
+                            int B, int H, int H_kv, int N, int d, bool causal,
+                            cudaStream_t stream);
+KC_API void launch_paged_attention(const float* Q, const int* block_table, const float* K_pool,
+                            const float* V_pool, float* O, const int* seq_lens,
+                            int B, int H, int H_kv, int d, int block_size, int max_blocks,
+                            cudaStream_t stream);
+KC_API void launch_verify_draft_tokens(const float* d_draft_probs, const float* d_target_probs,
+                                const int* d_draft_tokens, const float* d_rand_vals,
+                                const float* d_rand_vals2, int* d_accepted, int* d_corrected,
+                                int num_tokens, int vocab_size, cudaStream_t stream);
+
+/* ======================================================================= */
+/* Part 2: kc_* API                                                          */
+/* ======================================================================= */
+
+/* Non-synchronizing twin of launch_dequantize_int4 (quant_int4.cu:193). */
+KC_API int kc_dequantize_int4_f32(const uint8_t* packed, const float* scales, const uint8_t* zeros,
+                           float* out, int rows, int cols, int group_size, cudaStream_t stream);
+
+/* Non-synchronizing twin of launch_gemv_int4 (quant_int4.cu:221). */
+KC_API int kc_gemv_int4_f32(const uint8_t* packed, const float* scales, const uint8_t* zeros,
+                     const float* x, float* y, int rows, int cols, int group_size,
+                     cudaStream_t stream);
+
+/* GPTQ-style W4 (implicit zero-point 8, no zeros buffer):
+ * w[n,k] = (u - 8) * float(scales_f16[n, k/gs]), u the unsigned nibble
+ * (low nibble = even k).  Equals the reference dequant of (packed ^ 0x88) with
+ * zero points 0 (quant_int4.cu:99-104).  out bf16[N,K] = RNE(w). */
+KC_API int kc_dequantize_w4_bf16(const uint8_t* packed, const uint16_t* scales_f16, uint16_t* out_bf16,
+                          int N, int K, int group_size, cudaStream_t stream);
+
+/* W4A16 GEMV / skinny GEMM: y[m,n] = sum_k w[n,k] * x[m,k] for m < M <= 16;
+ * x bf16[M,K], y f32[M,N], fp32 accumulation.  Fast path: group_size % 128 == 0,
+ * K % 128 == 0, packed/x 16-byte aligned; other shapes take a CUDA-core path. */
+KC_API int kc_gemv_w4a16(const uint8_t* packed, const uint16_t* scales_f16, const uint16_t* x_bf16,
+                  float* y, int M, int N, int K, int group_size, cudaStream_t stream);
+
+/* One problem of a grouped W4A16 GEMV launch. */
+typedef struct kc_w4a16_problem {
+    const uint8_t*  packed;      /* u8[N, K/2]          */
+    const uint16_t* scales_f16;  /* f16[N, K/group]     */
+    const uint16_t* x_bf16;      /* bf16[M, K]          */
+    float*          y;           /* f32[M, N]           */
+    int N, K;
+} kc_w4a16_problem;
+
+/* All problems share M and group_size; one kernel launch covers them all
+ * (e.g. the QKV, O, gate+up and down projections of a decoder layer).
+ * count <= KC_W4A16_MAX_PROBLEMS. */
+#define KC_W4A16_MAX_PROBLEMS 8
+KC_API int kc_gemv_w4a16_grouped(const kc_w4a16_problem* problems, int count, int M,
+                          int group_size, cudaStream_t stream);
+
+/* FP8 E4M3 per-token quantization (fp8_quant.cu:89-131 semantics, bit-exact):
+ * scales[r] = amax_r > 0 ? amax_r/448 : 1; q = e4m3_satfinite(clamp(x/scale)). */
+KC_API int kc_quantize_fp8_per_token(const float* in, int8_t* out, float* scales,
+                              int rows, int cols, cudaStream_t stream);
+/* Per-output-channel weight quantization: the same arithmetic on W[N,K] rows. */
+KC_API int kc_quantize_fp8_per_channel(const float* w, int8_t* out, float* scales,
+                                int N, int K, cudaStream_t stream);
+/* Per-tensor quantization with the scale read from d_scale[0] on the device. */
+KC_API int kc_quantize_fp8_per_tensor(const float* in, int8_t* out, const float* d_scale,
+                               long count, cudaStream_t stream);
+/* Per-tensor quantization with the scale computed on the device:
+ * scale = amax(|x|) / 448 over the whole tensor (1 if amax == 0), written to
+ * scale_out[0]; the same value the reference's pybind path computes on the host
+ * (src/python/pybind_transformer.cpp:305-311).  workspace: >= 4 bytes of device
+ * memory, 4-byte aligned (cleared and used for the cross-CTA amax). */
+KC_API int kc_quantize_fp8_per_tensor_dynamic(const float* in, int8_t* out, float* scale_out,
+                                              long count, void* workspace, size_t workspace_bytes,
+                                              cudaStream_t stream);
+/* SmoothQuant divide fused into per-token quantization: bit-identical to
+ * launch_smoothquant_scale followed by launch_quantize_fp8(per_token=true),
+ * without the fp32 round trip through HBM. */
+KC_API int kc_smoothquant_quantize_fp8(const float* in, const float* smooth, int8_t* out,
+                                float* scales, int rows, int cols, cudaStream_t stream);
+/* Non-synchronizing twins of the reference's dequant / smoothquant launchers. */
+KC_API int kc_dequantize_fp8(const int8_t* in, const float* scales, float* out, int rows, int cols,
+                      bool per_token, cudaStream_t stream);
+KC_API int kc_smoothquant_scale(const float* in, const float* smooth, float* out, int rows, int cols,
+                         cudaStream_t stream);
+
+/* fp32 C[M,N] = A[M,K] * B[N,K]^T (the column/row-parallel shard GEMM). */
+KC_API int kc_sgemm_nt(const float* A, const float* B, float* C, int M, int N, int K,
+                cudaStream_t stream);
+
+/* --- NCCL, one process per GPU (the reference only has single-process
+ *     ncclCommInitAll, tensor_parallel_nccl.cu:58) --------------------------- */
+/* Size in bytes of the opaque unique id (128). */
+KC_API int kc_nccl_unique_id_bytes(void);
+/* Rank 0 creates the id (host buffer of kc_nccl_unique_id_bytes() bytes) and
+ * shares it with the other ranks out of band. */
+KC_API int kc_nccl_get_unique_id(void* out_id);
+/* Blocking communicator init on the current device; *comm is NULL on failure. */
+KC_API int kc_nccl_comm_init_rank(void** comm, int nranks, const void* id, int rank);
+KC_API int kc_nccl_comm_destroy(void* comm);
+/* Abandons in-flight work (use after a peer failed). */
+KC_API int kc_nccl_comm_abort(void* comm);
+/* KC_OK, or KC_ERR_NCCL if the communicator has an asynchronous error. */
+KC_API int kc_nccl_comm_check(void* comm);
+/* bf16 all-gather: recv = [send_0 | ... | send_{R-1}], count elements per rank. */
+KC_API int kc_allgather_bf16(void* comm, const uint16_t* send, uint16_t* recv, long count,
+                      cudaStream_t stream);
+/* bf16 / fp32 sum all-reduce (send == recv allowed). */
+KC_API int kc_allreduce_bf16(void* comm, const uint16_t* send, uint16_t* recv, long count,
+                      cudaStream_t stream);
+KC_API int kc_allreduce_f32(void* comm, const float* send, float* recv, long count,
+                     cudaStream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* KERNEL_CRAFT_H */

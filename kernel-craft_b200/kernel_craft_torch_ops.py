@@ -1,0 +1,234 @@
+"""
+kernel_craft_torch_ops -- torch-facing operators of the B200 quantized-linear library.
+
+Mirrors the quantized-linear part of kernel-craft's ctypes bridge
+(src/python/kernel_craft_torch_ops.py:265-381): same function names, argument
+meaning, return shapes and dtypes, and the same ``torch.ops.kernel_craft.*``
+registration (:428-471).  Each call hands ``data_ptr()``s and torch's current
+CUDA stream to the C ABI of libkernels.so (include/kernel_craft.h); there is no
+CPU path: the library must be built and the tensors must live on a CUDA device.
+
+Differences from the reference bridge, all on inputs the reference mishandles:
+  * ``fp8_quantize(x, per_token=False)`` computes the per-tensor scale
+    (amax/448) on the device, as the reference's pybind path does on the host
+    (src/python/pybind_transformer.cpp:305-311); the reference ctypes bridge
+    passes a zero scale (kernel_craft_torch_ops.py:347), which saturates
+    every code.
+  * invalid shapes raise ``KcError`` instead of launching.
+  * the reference's launchers synchronize the stream; these ops call the
+    non-synchronizing ``kc_*`` twins (results are ordered on the stream).
+
+New operators (no reference counterpart): ``w4a16_dequantize``,
+``w4a16_gemv``, ``w4a16_gemv_grouped``, ``fp8_quantize_per_channel``,
+``smoothquant_fp8_quantize``, ``smoothquant_scale``.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Sequence, Tuple
+
+import torch
+
+try:  # the reference's OTEL span helper, when it is on sys.path
+    from kernel_craft_otel import kernel_span  # type: ignore
+except ImportError:  # pragma: no cover
+    from contextlib import nullcontext as _nullcontext
+
+    def kernel_span(*_a, **_k):
+        return _nullcontext()
+
+import kc_lib
+from kc_lib import check, lib
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _require_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("kernel-craft ops take CUDA tensors only (no CPU path)")
+
+
+# ---------------------------------------------------------------------------
+# Reference operators (kernel_craft_torch_ops.py:265-381)
+# ---------------------------------------------------------------------------
+
+def int4_dequantize(packed, scales, zeros, rows: int, cols: int, group_size: int = 128):
+    """INT4 -> fp32 [rows, cols]; reference semantics (sign-extended nibbles,
+    unsigned zero points)."""
+    packed, scales, zeros = packed.contiguous(), scales.contiguous(), zeros.contiguous()
+    _require_cuda(packed, scales, zeros)
+    out = torch.empty(rows, cols, dtype=torch.float32, device=packed.device)
+    check(lib().kc_dequantize_int4_f32(_ptr(packed), _ptr(scales), _ptr(zeros), _ptr(out),
+                                       rows, cols, group_size, _stream()))
+    return out
+
+
+def int4_gemv(packed, scales, zeros, x, rows: int, cols: int, group_size: int = 128):
+    """y[rows] = W_int4 . x in fp32 (on-the-fly dequant)."""
+    packed, scales, zeros, x = (t.contiguous() for t in (packed, scales, zeros, x))
+    _require_cuda(packed, scales, zeros, x)
+    y = torch.empty(rows, dtype=torch.float32, device=packed.device)
+    with kernel_span("int4_gemv", rows=rows, cols=cols, group_size=group_size):
+        check(lib().kc_gemv_int4_f32(_ptr(packed), _ptr(scales), _ptr(zeros), _ptr(x), _ptr(y),
+                                     rows, cols, group_size, _stream()))
+    return y
+
+
+def fp8_quantize(x, per_token: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
+    """fp32 [rows, cols] -> (int8 E4M3 codes [rows, cols], fp32 scales [rows] or [1])."""
+    x = x.contiguous()
+    _require_cuda(x)
+    rows, cols = x.shape
+    q = torch.empty(rows, cols, dtype=torch.int8, device=x.device)
+    with kernel_span("fp8_quantize", rows=rows, cols=cols, per_token=per_token):
+        if per_token:
+            scales = torch.empty(rows, dtype=torch.float32, device=x.device)
+            check(lib().kc_quantize_fp8_per_token(_ptr(x), _ptr(q), _ptr(scales), rows, cols,
+                                                  _stream()))
+        else:
+            scales = torch.empty(1, dtype=torch.float32, device=x.device)
+            ws = torch.empty(1, dtype=torch.int32, device=x.device)
+            check(lib().kc_quantize_fp8_per_tensor_dynamic(_ptr(x), _ptr(q), _ptr(scales),
+                                                           rows * cols, _ptr(ws), 4, _stream()))
+    return q, scales
+
+
+def fp8_dequantize(q, scales, rows: int, cols: int, per_token: bool = True):
+    """int8 E4M3 codes -> fp32 [rows, cols]."""
+    q, scales = q.contiguous(), scales.contiguous()
+    _require_cuda(q, scales)
+    out = torch.empty(rows, cols, dtype=torch.float32, device=q.device)
+    check(lib().kc_dequantize_fp8(_ptr(q), _ptr(scales), _ptr(out), rows, cols, per_token,
+                                  _stream()))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# New operators
+# ---------------------------------------------------------------------------
+
+def smoothquant_scale(x, smooth):
+    """x[r, c] / smooth[c] (fp8_quant.cu:174-184 semantics)."""
+    x, smooth = x.contiguous(), smooth.contiguous()
+    _require_cuda(x, smooth)
+    rows, cols = x.shape
+    out = torch.empty_like(x)
+    check(lib().kc_smoothquant_scale(_ptr(x), _ptr(smooth), _ptr(out), rows, cols, _stream()))
+    return out
+
+
+def smoothquant_fp8_quantize(x, smooth) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Fused SmoothQuant divide + per-token FP8 quantization."""
+    x, smooth = x.contiguous(), smooth.contiguous()
+    _require_cuda(x, smooth)
+    rows, cols = x.shape
+    q = torch.empty(rows, cols, dtype=torch.int8, device=x.device)
+    scales = torch.empty(rows, dtype=torch.float32, device=x.device)
+    check(lib().kc_smoothquant_quantize_fp8(_ptr(x), _ptr(smooth), _ptr(q), _ptr(scales), rows,
+                                            cols, _stream()))
+    return q, scales
+
+
+def fp8_quantize_per_channel(w) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel weight quantization of W[N, K]: one scale per row."""
+    w = w.contiguous()
+    _require_cuda(w)
+    n, k = w.shape
+    q = torch.empty(n, k, dtype=torch.int8, device=w.device)
+    scales = torch.empty(n, dtype=torch.float32, device=w.device)
+    check(lib().kc_quantize_fp8_per_channel(_ptr(w), _ptr(q), _ptr(scales), n, k, _stream()))
+    return q, scales
+
+
+def w4a16_dequantize(packed, scales_f16, group_size: int = 128):
+    """GPTQ W4 (implicit zero-point 8, fp16 scales) -> bf16 [N, K]."""
+    packed, scales_f16 = packed.contiguous(), scales_f16.contiguous()
+    _require_cuda(packed, scales_f16)
+    n, k = packed.shape[0], packed.shape[1] * 2
+    out = torch.empty(n, k, dtype=torch.bfloat16, device=packed.device)
+    check(lib().kc_dequantize_w4_bf16(_ptr(packed), _ptr(scales_f16), _ptr(out), n, k,
+                                      group_size, _stream()))
+    return out
+
+
+def w4a16_gemv(packed, scales_f16, x, group_size: int = 128):
+    """y[M, N] (fp32) = x[M, K] (bf16, M <= 16) . W^T with W the GPTQ W4 [N, K]."""
+    packed, scales_f16, x = packed.contiguous(), scales_f16.contiguous(), x.contiguous()
+    _require_cuda(packed, scales_f16, x)
+    if x.dim() == 1:
+        x = x.unsqueeze(0)
+    m, k = x.shape
+    n = packed.shape[0]
+    y = torch.empty(m, n, dtype=torch.float32, device=packed.device)
+    with kernel_span("w4a16_gemv", rows=n, cols=k, batch=m, group_size=group_size):
+        check(lib().kc_gemv_w4a16(_ptr(packed), _ptr(scales_f16), _ptr(x), _ptr(y), m, n, k,
+                                  group_size, _stream()))
+    return y
+
+
+def w4a16_gemv_grouped(problems: Sequence[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]],
+                       group_size: int = 128) -> List[torch.Tensor]:
+    """One launch over several (packed, scales_f16, x) problems sharing M."""
+    if not 1 <= len(problems) <= kc_lib.KC_W4A16_MAX_PROBLEMS:
+        raise ValueError("1..8 problems per grouped launch")
+    arr = (kc_lib.W4A16Problem * len(problems))()
+    outs, keep = [], []
+    m = None
+    for i, (packed, scales, x) in enumerate(problems):
+        packed, scales, x = packed.contiguous(), scales.contiguous(), x.contiguous()
+        _require_cuda(packed, scales, x)
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        m = x.shape[0] if m is None else m
+        if x.shape[0] != m:
+            raise ValueError("all problems of a grouped launch share M")
+        n, k = packed.shape[0], packed.shape[1] * 2
+        y = torch.empty(m, n, dtype=torch.float32, device=packed.device)
+        arr[i] = kc_lib.W4A16Problem(packed.data_ptr(), scales.data_ptr(), x.data_ptr(),
+                                     y.data_ptr(), n, k)
+        outs.append(y)
+        keep += [packed, scales, x]
+    check(lib().kc_gemv_w4a16_grouped(arr, len(problems), m, group_size, _stream()))
+    return outs
+
+
+# ---------------------------------------------------------------------------
+# torch.library registration (kernel_craft_torch_ops.py:428-471)
+# ---------------------------------------------------------------------------
+
+def _register_torch_library() -> None:
+    libdef = torch.library.Library("kernel_craft", "DEF")
+    libdef.define("int4_dequantize(Tensor packed, Tensor scales, Tensor zeros, "
+                  "int rows, int cols, int group_size) -> Tensor")
+    libdef.define("int4_gemv(Tensor packed, Tensor scales, Tensor zeros, "
+                  "Tensor x, int rows, int cols, int group_size) -> Tensor")
+    libdef.define("fp8_quantize(Tensor x, bool per_token) -> (Tensor, Tensor)")
+    libdef.define("fp8_dequantize(Tensor q, Tensor scales, int rows, int cols, bool per_token) "
+                  "-> Tensor")
+    libdef.define("w4a16_gemv(Tensor packed, Tensor scales_f16, Tensor x, int group_size) -> Tensor")
+    libdef.define("w4a16_dequantize(Tensor packed, Tensor scales_f16, int group_size) -> Tensor")
+    libdef.define("fp8_quantize_per_channel(Tensor w) -> (Tensor, Tensor)")
+    libdef.define("smoothquant_fp8_quantize(Tensor x, Tensor smooth) -> (Tensor, Tensor)")
+    impl = torch.library.Library("kernel_craft", "IMPL")
+    for name, fn in (("int4_dequantize", int4_dequantize), ("int4_gemv", int4_gemv),
+                     ("fp8_quantize", fp8_quantize), ("fp8_dequantize", fp8_dequantize),
+                     ("w4a16_gemv", w4a16_gemv), ("w4a16_dequantize", w4a16_dequantize),
+                     ("fp8_quantize_per_channel", fp8_quantize_per_channel),
+                     ("smoothquant_fp8_quantize", smoothquant_fp8_quantize)):
+        impl.impl(name, fn, "CUDA")
+    globals()["_torch_lib_def"] = libdef
+    globals()["_torch_lib_impl"] = impl
+
+
+try:
+    _register_torch_library()
+    TORCH_OPS_REGISTERED = True
+except Exception:  # pragma: no cover - e.g. the namespace is already taken
+    TORCH_OPS_REGISTERED = False

@@ -1,0 +1,227 @@
+"""GPU parity: INT4 dequant and the W4 GEMV family vs the oracle (and the
+reference's own kernels when oracle/_ref/libkcref.so is present).
+
+Bars (written here, from the task's parity rules):
+  * dequantized weights (fp32 reference ABI, bf16 GPTQ API): bit-exact;
+  * GEMV outputs (fp32 accumulation): normwise max|y-ref|/max|ref| <= 1e-3,
+    and the reference C++ test's own bound (|err| < 1e-4) on its 16x16 KAT.
+"""
+import numpy as np
+import pytest
+import torch
+
+import kc_lib
+import kcref
+import oracle as O
+from kc_testutil import dev, host, last_error, misaligned, normwise_err, ptr, stream
+
+pytestmark = pytest.mark.gpu
+GEMV_TOL = 1e-3
+
+
+def _ref_int4_case(rows, cols, gs, zeros_mode, seed):
+    rng = np.random.default_rng(seed)
+    packed = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+    scales = rng.uniform(0.002, 0.02, (rows, cols // gs)).astype(np.float32)
+    G = cols // gs
+    zc = max(1, -(-G // 2))            # ceil, as the reference tests allocate
+    if zeros_mode == "zero":
+        zeros = np.zeros((rows, zc), np.uint8)
+    elif zeros_mode == "eight":
+        zeros = np.full((rows, zc), 0x88, np.uint8)
+    else:
+        zeros = rng.integers(0, 256, (rows, zc), dtype=np.uint8)
+    x = rng.standard_normal(cols).astype(np.float32)
+    return packed, scales, zeros, x
+
+
+def _launch_dequant(packed, scales, zeros, rows, cols, gs):
+    out = torch.full((rows, cols), float("nan"), dtype=torch.float32, device=packed.device)
+    kc_lib.lib().launch_dequantize_int4(ptr(packed), ptr(scales), ptr(zeros), ptr(out), rows, cols,
+                                        gs, stream())
+    kc_lib.check_last()
+    return out
+
+
+def _launch_gemv(packed, scales, zeros, x, rows, cols, gs):
+    y = torch.full((rows,), float("nan"), dtype=torch.float32, device=packed.device)
+    kc_lib.lib().launch_gemv_int4(ptr(packed), ptr(scales), ptr(zeros), ptr(x), ptr(y), rows, cols,
+                                  gs, stream())
+    kc_lib.check_last()
+    return y
+
+
+# ------------------------------------------------------- reference ABI -------
+def test_reference_kats(cuda, golden):
+    d = golden("kat_quant_int4.npz")
+    out = _launch_dequant(dev(d["deq4x8_packed"]), dev(d["deq4x8_scales"]), dev(d["deq4x8_zeros"]),
+                          4, 8, 8)
+    np.testing.assert_array_equal(host(out), d["deq4x8_expected"])
+    out = _launch_dequant(dev(d["mg_packed"]), dev(d["mg_scales"]), dev(d["mg_zeros"]), 4, 128, 64)
+    np.testing.assert_array_equal(host(out), d["mg_expected"])
+    y = _launch_gemv(dev(d["gemv16_packed"]), dev(d["gemv16_scales"]), dev(d["gemv16_zeros"]),
+                     dev(d["gemv16_x"]), 16, 16, 8)
+    assert np.max(np.abs(host(y) - d["gemv16_expected"])) < 1e-4      # test_quant_int4.cpp:142
+    t = golden("kat_triton_int4.npz")
+    for tag in ("small", "medium", "gs64"):
+        rows, cols, gs = (int(v) for v in t[f"tri_{tag}_shape"])
+        y = _launch_gemv(dev(t[f"tri_{tag}_packed"]), dev(t[f"tri_{tag}_scales"]),
+                         dev(t[f"tri_{tag}_zeros"]), dev(t[f"tri_{tag}_x"]), rows, cols, gs)
+        assert normwise_err(host(y), t[f"tri_{tag}_expected"]) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("rows,cols,gs", [(4096, 4096, 128), (37, 384, 128), (16, 96, 32),
+                                          (8, 256, 64), (5, 24, 8), (3, 6, 2), (1, 2, 2),
+                                          (64, 1536, 512)])
+@pytest.mark.parametrize("zeros_mode", ["zero", "eight", "random"])
+def test_dequant_and_gemv_reference_abi(cuda, rows, cols, gs, zeros_mode):
+    packed, scales, zeros, x = _ref_int4_case(rows, cols, gs, zeros_mode, seed=rows + cols)
+    dp, ds, dz, dx = dev(packed), dev(scales), dev(zeros), dev(x)
+    want = O.dequantize_int4(packed, scales, zeros, rows, cols, gs)
+    got = host(_launch_dequant(dp, ds, dz, rows, cols, gs))
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    y = host(_launch_gemv(dp, ds, dz, dx, rows, cols, gs))
+    assert normwise_err(y, O.gemv_int4(packed, scales, zeros, x, rows, cols, gs)) <= GEMV_TOL
+    if kcref.available():
+        ref_out = host(kcref.dequantize_int4(dp, ds, dz, rows, cols, gs))
+        np.testing.assert_array_equal(got.view(np.uint32), ref_out.view(np.uint32))
+        ref_y = host(kcref.gemv_int4(dp, ds, dz, dx, rows, cols, gs))
+        assert normwise_err(y, ref_y) <= GEMV_TOL
+
+
+def test_reference_abi_unaligned_pointers(cuda):
+    rows, cols, gs = 33, 512, 128
+    packed, scales, zeros, x = _ref_int4_case(rows, cols, gs, "random", 11)
+    dp = misaligned(dev(packed), 4)
+    dx = misaligned(dev(x), 4)
+    got = host(_launch_dequant(dp, dev(scales), dev(zeros), rows, cols, gs))
+    np.testing.assert_array_equal(got, O.dequantize_int4(packed, scales, zeros, rows, cols, gs))
+    y = host(_launch_gemv(dp, dev(scales), dev(zeros), dx, rows, cols, gs))
+    assert normwise_err(y, O.gemv_int4(packed, scales, zeros, x, rows, cols, gs)) <= GEMV_TOL
+
+
+def test_reference_abi_rejects_bad_shapes(cuda):
+    l = kc_lib.lib()
+    buf = torch.zeros(64, dtype=torch.float32, device=cuda)
+    sentinel = buf.clone()
+    last_error()
+    l.launch_dequantize_int4(ptr(buf), ptr(buf), ptr(buf), ptr(buf), 2, 7, 7, stream())  # odd cols
+    assert last_error()[0] == kc_lib.KC_ERR_INVALID_ARG
+    l.launch_gemv_int4(ptr(buf), ptr(buf), ptr(buf), ptr(buf), ptr(buf), 2, 8, 3, stream())  # gs !| cols
+    assert last_error()[0] == kc_lib.KC_ERR_INVALID_ARG
+    l.launch_dequantize_int4(ptr(buf), ptr(buf), ptr(buf), ptr(buf), 2, 8, 0, stream())  # gs == 0
+    assert last_error()[0] == kc_lib.KC_ERR_INVALID_ARG
+    torch.cuda.synchronize()
+    assert torch.equal(buf, sentinel)
+
+
+def test_empty_shapes(cuda):
+    z = torch.zeros(16, dtype=torch.uint8, device=cuda)
+    f = torch.zeros(16, dtype=torch.float32, device=cuda)
+    kc_lib.check(kc_lib.lib().kc_dequantize_int4_f32(ptr(z), ptr(f), ptr(z), ptr(f), 0, 128, 128,
+                                                     stream()))
+    kc_lib.check(kc_lib.lib().kc_gemv_int4_f32(ptr(z), ptr(f), ptr(z), ptr(f), ptr(f), 0, 128, 128,
+                                               stream()))
+
+
+# ------------------------------------------------------------ GPTQ W4A16 ----
+def _w4a16_inputs(M, N, K, gs, seed=0):
+    packed, scales = O.make_w4_gptq(N, K, gs, seed=seed)
+    x = O.make_activations_bf16(M, K, seed=seed + 1)
+    return packed, scales, x
+
+
+def _bf16_dev(bits):
+    return dev(bits).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("N,K,gs", [(256, 512, 128), (40, 384, 128), (17, 256, 256),
+                                    (64, 4096, 64), (33, 96, 32), (8, 128, 128)])
+def test_w4_bf16_dequant_bitexact(cuda, N, K, gs):
+    packed, scales, _ = _w4a16_inputs(1, N, K, gs, seed=N)
+    out = torch.empty(N, K, dtype=torch.bfloat16, device=cuda)
+    kc_lib.check(kc_lib.lib().kc_dequantize_w4_bf16(ptr(dev(packed)), ptr(dev(scales)), ptr(out),
+                                                    N, K, gs, stream()))
+    got = host(out.view(torch.int16)).view(np.uint16)
+    np.testing.assert_array_equal(got, O.dequantize_w4_bf16(packed, scales, N, K, gs))
+
+
+def _run_w4a16(packed, scales, x, M, N, K, gs):
+    y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda:0")
+    kc_lib.check(kc_lib.lib().kc_gemv_w4a16(ptr(dev(packed)), ptr(dev(scales)), ptr(_bf16_dev(x)),
+                                            ptr(y), M, N, K, gs, stream()))
+    return host(y)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 8, 9, 16])
+@pytest.mark.parametrize("N,K,gs", [(256, 1024, 128), (100, 384, 128), (16, 128, 128),
+                                    (48, 2048, 256), (24, 256, 64), (7, 96, 32)])
+def test_w4a16_gemv_small(cuda, M, N, K, gs):
+    packed, scales, x = _w4a16_inputs(M, N, K, gs, seed=M * 7 + N)
+    y = _run_w4a16(packed, scales, x, M, N, K, gs)
+    assert normwise_err(y, O.gemv_w4a16(packed, scales, x, M, N, K, gs)) <= GEMV_TOL
+
+
+@pytest.mark.parametrize("K,N", [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)])
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_w4a16_gemv_7b_shapes(cuda, K, N, M):
+    """Config 2 shapes at full size; the oracle checks a seeded sample of 96 rows."""
+    gs = 128
+    packed, scales, x = _w4a16_inputs(M, N, K, gs, seed=K + N + M)
+    y = _run_w4a16(packed, scales, x, M, N, K, gs)
+    rows = np.sort(np.random.default_rng(0).choice(N, 96, replace=False))
+    rows[0], rows[-1] = 0, N - 1
+    ref = O.gemv_w4a16(packed[rows], scales[rows], x, M, len(rows), K, gs)
+    assert normwise_err(y[:, rows], ref) <= GEMV_TOL
+    assert np.all(np.isfinite(y))
+
+
+def test_w4a16_grouped_matches_single(cuda):
+    gs, M = 128, 4
+    shapes = [(4096, 1536), (4096, 512), (1024, 2752), (1376, 512)]   # (K, N)
+    import kernel_craft_torch_ops as ops
+    probs, singles = [], []
+    for i, (K, N) in enumerate(shapes):
+        packed, scales, x = _w4a16_inputs(M, N, K, gs, seed=100 + i)
+        dp, ds, dx = dev(packed), dev(scales).view(torch.float16), _bf16_dev(x)
+        probs.append((dp, ds, dx))
+        singles.append(host(ops.w4a16_gemv(dp, ds, dx, gs)))
+    outs = ops.w4a16_gemv_grouped(probs, gs)
+    for y, s in zip(outs, singles):
+        np.testing.assert_array_equal(host(y), s)
+
+
+def test_w4a16_unaligned_takes_scalar_path(cuda):
+    M, N, K, gs = 3, 40, 256, 128
+    packed, scales, x = _w4a16_inputs(M, N, K, gs, seed=5)
+    dp = misaligned(dev(packed), 4)
+    y = torch.empty(M, N, dtype=torch.float32, device=cuda)
+    kc_lib.check(kc_lib.lib().kc_gemv_w4a16(ptr(dp), ptr(dev(scales)), ptr(_bf16_dev(x)), ptr(y),
+                                            M, N, K, gs, stream()))
+    assert normwise_err(host(y), O.gemv_w4a16(packed, scales, x, M, N, K, gs)) <= GEMV_TOL
+
+
+def test_w4a16_rejects_bad_args(cuda):
+    l = kc_lib.lib()
+    b = torch.zeros(1024, dtype=torch.uint8, device=cuda)
+    with pytest.raises(kc_lib.KcError):
+        kc_lib.check(l.kc_gemv_w4a16(ptr(b), ptr(b), ptr(b), ptr(b), 17, 16, 128, 128, stream()))
+    with pytest.raises(kc_lib.KcError):
+        kc_lib.check(l.kc_gemv_w4a16(ptr(b), ptr(b), ptr(b), ptr(b), 1, 16, 100, 128, stream()))
+    with pytest.raises(kc_lib.KcError):
+        kc_lib.check(l.kc_gemv_w4a16(ptr(b), ptr(b), ptr(b), ptr(b), 0, 16, 128, 128, stream()))
+
+
+def test_torch_ops_mirror(cuda):
+    """The reference bridge's operator names and shapes (kernel_craft_torch_ops.py:265-381)."""
+    import kernel_craft_torch_ops as ops
+    rows, cols, gs = 64, 1024, 128
+    packed, scales, zeros, x = _ref_int4_case(rows, cols, gs, "zero", 3)
+    out = ops.int4_dequantize(dev(packed), dev(scales), dev(zeros), rows, cols, gs)
+    assert out.shape == (rows, cols) and out.dtype == torch.float32
+    np.testing.assert_array_equal(host(out), O.dequantize_int4(packed, scales, zeros, rows, cols, gs))
+    y = ops.int4_gemv(dev(packed), dev(scales), dev(zeros), dev(x), rows, cols, gs)
+    assert y.shape == (rows,)
+    assert normwise_err(host(y), O.gemv_int4(packed, scales, zeros, x, rows, cols, gs)) <= GEMV_TOL
+    y2 = torch.ops.kernel_craft.int4_gemv(dev(packed), dev(scales), dev(zeros), dev(x), rows, cols, gs)
+    np.testing.assert_array_equal(host(y2), host(y))

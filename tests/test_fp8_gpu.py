@@ -62,7 +62,8 @@ def test_config1_outliers_bitexact(cuda):
     w = O.make_weight_f32(256, 8192, seed=2)
     qw = torch.empty(256, 8192, dtype=torch.int8, device=cuda)
     sw = torch.empty(256, dtype=torch.float32, device=cuda)
-    kc_lib.check(kc_lib.lib().kc_quantize_fp8_per_channel(ptr(dev(w)), ptr(qw), ptr(sw), 256, 8192,
+    dw = dev(w)
+    kc_lib.check(kc_lib.lib().kc_quantize_fp8_per_channel(ptr(dw), ptr(qw), ptr(sw), 256, 8192,
                                                           stream()))
     wq2, ws2 = O.quantize_fp8_per_token(w)
     np.testing.assert_array_equal(host(sw), ws2)
@@ -113,8 +114,8 @@ def test_dequant_bitexact(cuda, rows, cols, per_token):
     codes = rng.integers(0, 256, (rows, cols), dtype=np.uint8)
     scales = rng.uniform(0.001, 2.0, rows if per_token else 1).astype(np.float32)
     out = torch.empty(rows, cols, dtype=torch.float32, device=cuda)
-    kc_lib.lib().launch_dequantize_fp8(ptr(dev(codes)), ptr(dev(scales)), ptr(out), rows, cols,
-                                       per_token, stream())
+    dc, ds = dev(codes), dev(scales)   # keep the device copies alive across the call
+    kc_lib.lib().launch_dequantize_fp8(ptr(dc), ptr(ds), ptr(out), rows, cols, per_token, stream())
     kc_lib.check_last()
     got = host(out)
     want = O.dequantize_fp8(codes, scales, rows, cols, per_token)
@@ -133,14 +134,15 @@ def test_smoothquant_and_fused(cuda, rows, cols):
     x = O.make_outlier_activations(rows, cols, seed=cols)
     s = rng.uniform(0.5, 20.0, cols).astype(np.float32)
     out = torch.empty(rows, cols, dtype=torch.float32, device=cuda)
-    kc_lib.lib().launch_smoothquant_scale(ptr(dev(x)), ptr(dev(s)), ptr(out), rows, cols, stream())
+    dx, dsm = dev(x), dev(s)
+    kc_lib.lib().launch_smoothquant_scale(ptr(dx), ptr(dsm), ptr(out), rows, cols, stream())
     kc_lib.check_last()
     sm = O.smoothquant_scale(x, s)
     np.testing.assert_array_equal(host(out).view(np.uint32), sm.view(np.uint32))
     # fused divide + per-token quant == the two reference steps
     q = torch.empty(rows, cols, dtype=torch.int8, device=cuda)
     sc = torch.empty(rows, dtype=torch.float32, device=cuda)
-    kc_lib.check(kc_lib.lib().kc_smoothquant_quantize_fp8(ptr(dev(x)), ptr(dev(s)), ptr(q), ptr(sc),
+    kc_lib.check(kc_lib.lib().kc_smoothquant_quantize_fp8(ptr(dx), ptr(dsm), ptr(q), ptr(sc),
                                                           rows, cols, stream()))
     wq, ws = O.quantize_fp8_per_token(sm)
     np.testing.assert_array_equal(host(sc), ws)

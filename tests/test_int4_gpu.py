@@ -140,16 +140,16 @@ def _bf16_dev(bits):
 def test_w4_bf16_dequant_bitexact(cuda, N, K, gs):
     packed, scales, _ = _w4a16_inputs(1, N, K, gs, seed=N)
     out = torch.empty(N, K, dtype=torch.bfloat16, device=cuda)
-    kc_lib.check(kc_lib.lib().kc_dequantize_w4_bf16(ptr(dev(packed)), ptr(dev(scales)), ptr(out),
-                                                    N, K, gs, stream()))
+    dp, ds = dev(packed), dev(scales)   # keep the device copies alive across the call
+    kc_lib.check(kc_lib.lib().kc_dequantize_w4_bf16(ptr(dp), ptr(ds), ptr(out), N, K, gs, stream()))
     got = host(out.view(torch.int16)).view(np.uint16)
     np.testing.assert_array_equal(got, O.dequantize_w4_bf16(packed, scales, N, K, gs))
 
 
 def _run_w4a16(packed, scales, x, M, N, K, gs):
     y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda:0")
-    kc_lib.check(kc_lib.lib().kc_gemv_w4a16(ptr(dev(packed)), ptr(dev(scales)), ptr(_bf16_dev(x)),
-                                            ptr(y), M, N, K, gs, stream()))
+    dp, ds, dx = dev(packed), dev(scales), _bf16_dev(x)   # alive across the call
+    kc_lib.check(kc_lib.lib().kc_gemv_w4a16(ptr(dp), ptr(ds), ptr(dx), ptr(y), M, N, K, gs, stream()))
     return host(y)
 
 
@@ -196,8 +196,8 @@ def test_w4a16_unaligned_takes_scalar_path(cuda):
     packed, scales, x = _w4a16_inputs(M, N, K, gs, seed=5)
     dp = misaligned(dev(packed), 4)
     y = torch.empty(M, N, dtype=torch.float32, device=cuda)
-    kc_lib.check(kc_lib.lib().kc_gemv_w4a16(ptr(dp), ptr(dev(scales)), ptr(_bf16_dev(x)), ptr(y),
-                                            M, N, K, gs, stream()))
+    ds, dx = dev(scales), _bf16_dev(x)
+    kc_lib.check(kc_lib.lib().kc_gemv_w4a16(ptr(dp), ptr(ds), ptr(dx), ptr(y), M, N, K, gs, stream()))
     assert normwise_err(host(y), O.gemv_w4a16(packed, scales, x, M, N, K, gs)) <= GEMV_TOL
 
 

@@ -134,7 +134,7 @@ def test_fp8_per_token_reference_tests(golden):
     qz, sz = O.quantize_fp8_per_token(z)
     assert np.all(sz == 1.0) and np.all(O.dequantize_fp8(qz, sz, 4, 32, True) == 0)
     # binding test src/python/tests/test_transformer_bindings.py:213-221
-    xb = d["pt_in"] if "bind_fp8_in" not in golden("kat_bindings.npz") else golden("kat_bindings.npz")["bind_fp8_in"]
+    xb = golden("kat_bindings.npz")["bind_fp8_in"]
     qb, sb = O.quantize_fp8_per_token(xb)
     xbh = O.dequantize_fp8(qb, sb, *xb.shape, True)
     nzb = np.abs(xb) > 1e-6
@@ -220,7 +220,12 @@ def test_oracle_matches_reference_kernels_fp8():
         np.testing.assert_array_equal(s, d[f"{tag}_scales"])
         np.testing.assert_array_equal(q, d[f"{tag}_codes"].view(np.uint8))
         xh = O.dequantize_fp8(q, s, *x.shape, True)
-        np.testing.assert_array_equal(xh.view(np.uint32), d[f"{tag}_dequant"].view(np.uint32))
+        ref = d[f"{tag}_dequant"]
+        # NaN payloads differ between x86 (0xFFC00000) and the GPU (0x7FFFFFFF):
+        # compare the NaN positions, and the bits of everything else.
+        nan = np.isnan(ref)
+        np.testing.assert_array_equal(np.isnan(xh), nan)
+        np.testing.assert_array_equal(xh[~nan].view(np.uint32), ref[~nan].view(np.uint32))
 
 
 def test_oracle_matches_reference_kernels_int4():

@@ -53,6 +53,15 @@ KC_API int kc_get_last_error(void);
 KC_API const char* kc_get_last_error_string(void);
 /* Library version string. */
 KC_API const char* kc_version(void);
+/* Synchronizes the current device, then reads and clears the status words the
+ * pipelined kernels set when a bounded device-side wait gives up
+ * (KC_ERR_TIMEOUT); KC_OK when none did. */
+KC_API int kc_get_device_status(void);
+/* Test hook: one CTA waits on an mbarrier phase nothing completes; the wait
+ * gives up after timeout_ns (<= 5 s), records KC_ERR_TIMEOUT for
+ * kc_get_device_status() and writes the milliseconds waited to
+ * *waited_ms_device (device int).  The context stays usable. */
+KC_API int kc_selftest_bounded_wait(uint64_t timeout_ns, int* waited_ms_device, cudaStream_t stream);
 
 /* ======================================================================= */
 /* Part 1: reference launcher ABI (drop-in)                                 */

@@ -29,6 +29,11 @@ inline int check_launch(const char* what) { return check_cuda(cudaGetLastError()
 // Multiprocessor count of the current device (cached per device).
 int sm_count();
 
+// Device status words of the translation units with bounded device-side waits
+// (KC_DEFINE_STATUS_READER in sm100.cuh): 0 or the first status recorded.
+int read_device_status_int4(bool clear);
+int read_device_status_selftest(bool clear);
+
 __host__ __device__ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }

@@ -55,6 +55,18 @@ const char* kc_get_last_error_string(void) { return t_last_msg; }
 
 const char* kc_version(void) { return "kernel-craft-b200 0.1 (sm_100a)"; }
 
+int kc_get_device_status(void) {
+    // Synchronizes the device so every launched kernel has finished updating
+    // its unit's status word, then reads and clears all of them.
+    if (cudaDeviceSynchronize() != cudaSuccess)
+        return kc::set_error(KC_ERR_CUDA, "kc_get_device_status: device synchronize failed");
+    int st = KC_OK;
+    for (int v : {kc::read_device_status_int4(true), kc::read_device_status_selftest(true)})
+        if (st == KC_OK && v != KC_OK) st = v;
+    if (st != KC_OK) kc::set_error(st, "a device-side wait gave up (status %d)", st);
+    return st;
+}
+
 // --- launchers outside this library's scope --------------------------------
 // src/python/kernel_craft_torch_ops.py:105-168 resolves these three symbols
 // when it loads libkernels.so; exporting them lets the unmodified bridge load.

@@ -49,6 +49,8 @@ _PROTOS = [
     ("kc_get_last_error", ci, []),
     ("kc_get_last_error_string", ctypes.c_char_p, []),
     ("kc_version", ctypes.c_char_p, []),
+    ("kc_get_device_status", ci, []),
+    ("kc_selftest_bounded_wait", ci, [ctypes.c_uint64, vp, vp]),
     # reference ABI
     ("launch_dequantize_int4", None, [vp, vp, vp, vp, ci, ci, ci, vp]),
     ("launch_gemv_int4", None, [vp, vp, vp, vp, vp, ci, ci, ci, vp]),

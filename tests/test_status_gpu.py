@@ -1,0 +1,40 @@
+"""Failure detection without a GPU fault: a device-side wait that nothing
+completes gives up after a short limit, the kernel returns, the host reads
+KC_ERR_TIMEOUT, and the context keeps working."""
+import numpy as np
+import pytest
+import torch
+
+import kc_lib
+import oracle as O
+from kc_testutil import host, ptr, stream
+
+pytestmark = pytest.mark.gpu
+
+
+def test_bounded_wait_times_out_and_context_survives(cuda):
+    l = kc_lib.lib()
+    assert l.kc_get_device_status() == kc_lib.KC_OK
+    waited = torch.full((1,), -7, dtype=torch.int32, device=cuda)
+    kc_lib.check(l.kc_selftest_bounded_wait(200_000_000, ptr(waited), stream()))   # 0.2 s
+    assert l.kc_get_device_status() == kc_lib.KC_ERR_TIMEOUT
+    assert 200 <= int(host(waited)[0]) < 5000
+    assert l.kc_get_device_status() == kc_lib.KC_OK          # reading cleared it
+    # the context is still usable: a real kernel runs and is correct
+    import kernel_craft_torch_ops as ops
+    packed, scales = O.make_w4_gptq(64, 256, 128, seed=1)
+    x = O.make_activations_bf16(1, 256, seed=2)
+    y = ops.w4a16_gemv(torch.from_numpy(packed).to(cuda), torch.from_numpy(scales).to(cuda),
+                       torch.from_numpy(x).to(cuda).view(torch.bfloat16), 128)
+    ref = O.gemv_w4a16(packed, scales, x, 1, 64, 256, 128)
+    assert np.max(np.abs(host(y) - ref)) / np.max(np.abs(ref)) <= 1e-3
+
+
+def test_pipelined_gemv_reports_no_timeout(cuda):
+    import kernel_craft_torch_ops as ops
+    packed, scales = O.make_w4_gptq(4096, 4096, 128, seed=3)
+    x = O.make_activations_bf16(1, 4096, seed=4)
+    for _ in range(3):
+        ops.w4a16_gemv(torch.from_numpy(packed).to(cuda), torch.from_numpy(scales).to(cuda),
+                       torch.from_numpy(x).to(cuda).view(torch.bfloat16), 128)
+    assert kc_lib.lib().kc_get_device_status() == kc_lib.KC_OK

@@ -31,7 +31,7 @@ int sm_count();
 
 // Device status words of the translation units with bounded device-side waits
 // (KC_DEFINE_STATUS_READER in sm100.cuh): 0 or the first status recorded.
-int read_device_status_int4(bool clear);
+int read_device_status_gemv(bool clear);
 int read_device_status_selftest(bool clear);
 
 __host__ __device__ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -72,6 +72,19 @@ __device__ __forceinline__ uint4 kc_ldg_keep(const void* p) {
     asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
+    return v;
+}
+
+// Predicated 128-bit read-only load: zeros when !pred, no branch.
+__device__ __forceinline__ uint4 kc_ldg_keep_if(const void* p, bool pred) {
+    uint4 v;
+    asm volatile(
+        "{\n\t.reg .pred q;\n\t"
+        "setp.ne.b32 q, %5, 0;\n\t"
+        "mov.b32 %0, 0; mov.b32 %1, 0; mov.b32 %2, 0; mov.b32 %3, 0;\n\t"
+        "@q ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n\t}"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p), "r"((int)pred));
     return v;
 }
 

@@ -216,6 +216,16 @@ KC_API int kc_dequantize_fp8(const int8_t* in, const float* scales, float* out, 
 KC_API int kc_smoothquant_scale(const float* in, const float* smooth, float* out, int rows, int cols,
                          cudaStream_t stream);
 
+/* FP8 E4M3 W8A8 GEMM on the tcgen05 tensor cores:
+ * out[m, n] = (sum_k e4m3(a[m,k]) * e4m3(w[n,k])) * sa[m] * sw[n], fp32 accumulation,
+ * written as bf16 (out_f32 = 0) or fp32 (out_f32 = 1) with row pitch ldc (elements).
+ * a_codes int8[M, K] and w_codes int8[N, K] are the E4M3 bit patterns that
+ * kc_quantize_fp8_per_token / kc_quantize_fp8_per_channel (and the reference's
+ * launch_quantize_fp8, fp8_quant.cu:201) produce.  Requires K % 16 == 0,
+ * N % 8 == 0, ldc % 8 == 0 and 16-byte aligned codes, sw and out. */
+KC_API int kc_gemm_fp8(const int8_t* a_codes, const float* sa, const int8_t* w_codes, const float* sw,
+                       void* out, int out_f32, int M, int N, int K, int ldc, cudaStream_t stream);
+
 /* fp32 C[M,N] = A[M,K] * B[N,K]^T (the column/row-parallel shard GEMM). */
 KC_API int kc_sgemm_nt(const float* A, const float* B, float* C, int M, int N, int K,
                 cudaStream_t stream);

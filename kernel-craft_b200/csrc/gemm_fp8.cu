@@ -1,0 +1,256 @@
+// gemm_fp8.cu -- FP8 E4M3 W8A8 GEMM on the 5th-generation tensor cores (sm_100a).
+//
+// C[m, n] = bf16( (sum_k e4m3(A[m, k]) * e4m3(W[n, k])) * sa[m] * sw[n] )
+// A: per-token quantized activations (codes [M, K], scales sa[M]), W: per-output-
+// channel quantized weights (codes [N, K], scales sw[N]), both K-major as the
+// reference's quantizer writes them (src/kernels/transformer/fp8_quant.cu);
+// fp32 accumulation in TMEM; bf16 output, or fp32 when requested.
+//
+// One persistent CTA per SM walks 128 x 256 output tiles.  Warp roles:
+//   warp 0  TMA producer: 128 x 128-byte A and 256 x 128-byte W boxes per k-step
+//           into a 4-stage ring (128-byte swizzle), completion on "full" mbarriers;
+//   warp 1  allocates 512 TMEM columns (two 128 x 256 fp32 accumulators) and one
+//           lane issues tcgen05.mma kind::f8f6f4 (M 128, N 256, K 32) four times
+//           per stage, releasing the stage with tcgen05.commit on its "empty"
+//           mbarrier and a finished accumulator on "tmem_full";
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time from the warp's 32 TMEM
+//           lanes, scale by sa[m] * sw[n], convert, store; then free the
+//           accumulator ("tmem_empty") so the MMA of tile i+2 can start while
+//           tile i+1 accumulates.
+// No TMA multicast is used (the kernel also runs inside multi-GPU jobs).
+#include <algorithm>
+
+#include "kc_common.cuh"
+#include "sm100.cuh"
+#include "tensor_map.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 128;   // BK in bytes = e4m3 elements
+constexpr int kStages = 4;
+constexpr int kABytes = BM * BK;              // 16 KB
+constexpr int kBBytes = BN * BK;              // 32 KB
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+constexpr uint32_t kTmemCols = 512;
+
+struct alignas(64) Params {
+    CUtensorMap amap;   // A codes {K, M}, box {128, 128}, 128-byte swizzle
+    CUtensorMap wmap;   // W codes {K, N}, box {128, 256}, 128-byte swizzle
+    const float* sa;
+    const float* sw;
+    void* out;          // bf16 or fp32 [M, ldc]
+    int M, N, K, ldc;
+    int out_f32;
+    int tiles_m, tiles_n;
+};
+
+struct Smem {
+    uint8_t a[kStages][kABytes];   // 1024-byte aligned (swizzle atoms)
+    uint8_t b[kStages][kBBytes];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_constant__ Params P) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled operand tiles
+    const uint32_t raw = sm100::smem_u32(smem_raw);
+    Smem& S = *reinterpret_cast<Smem*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles = P.tiles_m * P.tiles_n;
+    const int kblocks = (P.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            sm100::mbar_init(&S.full[i], 1);
+            sm100::mbar_init(&S.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            sm100::mbar_init(&S.tmem_full[i], 1);
+            sm100::mbar_init(&S.tmem_empty[i], kEpiWarps);
+        }
+        sm100::mbar_init(&S.drain, 1);
+        S.abort = 0;
+        sm100::fence_barrier_init();
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(&S.tmem_base, kTmemCols);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = S.tmem_base;
+    volatile int* abort = &S.abort;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer -----------------------------
+        if (lane == 0) {
+            sm100::prefetch_tensormap(&P.amap);
+            sm100::prefetch_tensormap(&P.wmap);
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                const int m0 = (tile % P.tiles_m) * BM, n0 = (tile / P.tiles_m) * BN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+                    sm100::mbar_wait_or_abort(&S.empty[s], ph ^ 1u, abort);
+                    sm100::mbar_arrive_expect_tx(&S.full[s], kABytes + kBBytes);
+                    sm100::tma_load_2d(S.a[s], &P.amap, kb * BK, m0, &S.full[s]);
+                    sm100::tma_load_2d(S.b[s], &P.wmap, kb * BK, n0, &S.full[s]);
+                }
+            }
+            // drain: the last copies land before the CTA may exit (bounded)
+            for (uint32_t j = it > (uint32_t)kStages ? it - kStages : 0u; j < it; ++j)
+                sm100::mbar_wait(&S.full[j % kStages], (j / kStages) & 1u, 200000000ull);
+        }
+    } else if (warp == 1) {
+        // ------------------------------- MMA issuer -------------------------------
+        if (lane == 0) {
+            const uint32_t idesc = sm100::umma_idesc(sm100::kFmtE4M3, sm100::kFmtE4M3, BM, BN);
+            uint32_t it = 0, t = 0;
+            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+                const uint32_t acc = t & 1u;
+                sm100::mbar_wait_or_abort(&S.tmem_empty[acc], ((t >> 1) & 1u) ^ 1u, abort);
+                sm100::tc_fence_after();
+                const uint32_t d = tmem + acc * BN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+                    sm100::mbar_wait_or_abort(&S.full[s], ph, abort);
+                    sm100::tc_fence_after();
+                    const uint64_t adesc = sm100::umma_desc_sw128(sm100::smem_u32(S.a[s]));
+                    const uint64_t bdesc = sm100::umma_desc_sw128(sm100::smem_u32(S.b[s]));
+#pragma unroll
+                    for (int j = 0; j < BK / 32; ++j)  // K = 32 per instruction (32 bytes)
+                        sm100::umma_f8f6f4_ss(d, adesc + 2 * j, bdesc + 2 * j, idesc,
+                                              (kb | j) != 0 ? 1u : 0u);
+                    sm100::tc_commit(&S.empty[s]);  // stage free once these MMAs retire
+                }
+                sm100::tc_commit(&S.tmem_full[acc]);  // accumulator complete
+            }
+            // drain: every MMA this thread issued retires before TMEM is freed
+            sm100::tc_commit(&S.drain);
+            sm100::mbar_wait(&S.drain, 0, 200000000ull);
+        }
+    } else {
+        // -------------------------------- epilogue --------------------------------
+        const int q = warp & 3;                      // TMEM lane quarter of this warp
+        uint32_t t = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+            const uint32_t acc = t & 1u;
+            const int m0 = (tile % P.tiles_m) * BM, n0 = (tile / P.tiles_m) * BN;
+            const int m = m0 + q * 32 + lane;
+            const float sam = (m < P.M) ? __ldg(P.sa + m) : 0.f;
+            sm100::mbar_wait_or_abort(&S.tmem_full[acc], (t >> 1) & 1u, abort);
+            sm100::tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, r);
+                sm100::tmem_wait_ld();
+                const int nb = n0 + c * 32;
+                if (m >= P.M || nb >= P.N) continue;
+                const float4* swv = reinterpret_cast<const float4*>(P.sw + nb);
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 s4 = (nb + 4 * i + 3 < P.N) ? __ldg(swv + i)
+                                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                    v[4 * i + 0] = __uint_as_float(r[4 * i + 0]) * sam * s4.x;
+                    v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) * sam * s4.y;
+                    v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) * sam * s4.z;
+                    v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) * sam * s4.w;
+                }
+                if (P.out_f32) {
+                    float* o = reinterpret_cast<float*>(P.out) + (size_t)m * P.ldc + nb;
+                    if (nb + 32 <= P.N) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            reinterpret_cast<float4*>(o)[i] =
+                                make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    } else {
+                        for (int i = 0; i < 32 && nb + i < P.N; ++i) o[i] = v[i];
+                    }
+                } else {
+                    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(P.out) + (size_t)m * P.ldc + nb;
+                    if (nb + 32 <= P.N) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            reinterpret_cast<uint4*>(o)[i] =
+                                make_uint4(bf16x2_bits(v[8 * i], v[8 * i + 1]),
+                                           bf16x2_bits(v[8 * i + 2], v[8 * i + 3]),
+                                           bf16x2_bits(v[8 * i + 4], v[8 * i + 5]),
+                                           bf16x2_bits(v[8 * i + 6], v[8 * i + 7]));
+                    } else {
+                        for (int i = 0; i < 32 && nb + i < P.N; ++i) o[i] = __float2bfloat16_rn(v[i]);
+                    }
+                }
+            }
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&S.tmem_empty[acc]);
+        }
+    }
+
+    // teardown: every MMA has been consumed by the epilogue before this barrier
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace
+
+KC_DEFINE_STATUS_READER(gemm_fp8)
+
+extern "C" {
+
+int kc_gemm_fp8(const int8_t* a_codes, const float* sa, const int8_t* w_codes, const float* sw,
+                void* out, int out_f32, int M, int N, int K, int ldc, cudaStream_t stream) {
+    KC_REQUIRE(a_codes && sa && w_codes && sw && out, KC_ERR_INVALID_ARG, "null pointer argument");
+    KC_REQUIRE(M >= 0 && N >= 0 && K >= 0, KC_ERR_INVALID_ARG, "negative size");
+    if (M == 0 || N == 0) return KC_OK;
+    KC_REQUIRE(K > 0 && K % 16 == 0, KC_ERR_INVALID_ARG, "K=%d must be a positive multiple of 16", K);
+    KC_REQUIRE(N % 8 == 0 && ldc >= N && ldc % 8 == 0, KC_ERR_INVALID_ARG,
+               "N=%d and ldc=%d must be multiples of 8 with ldc >= N", N, ldc);
+    KC_REQUIRE(kc::aligned(a_codes, 16) && kc::aligned(w_codes, 16) && kc::aligned(out, 16) &&
+                   kc::aligned(sw, 16),
+               KC_ERR_ALIGNMENT, "operands must be 16-byte aligned");
+    Params P{};
+    int st = kc::encode_2d(&P.amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_codes, (uint64_t)K, (uint64_t)M,
+                           (uint64_t)K, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = kc::encode_2d(&P.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes, (uint64_t)K, (uint64_t)N,
+                       (uint64_t)K, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    P.sa = sa;
+    P.sw = sw;
+    P.out = out;
+    P.M = M;
+    P.N = N;
+    P.K = K;
+    P.ldc = ldc;
+    P.out_f32 = out_f32 ? 1 : 0;
+    P.tiles_m = (M + BM - 1) / BM;
+    P.tiles_n = (N + BN - 1) / BN;
+    const size_t smem = sizeof(Smem) + 1024;
+    KC_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem),
+                "gemm_fp8 shared-memory attribute");
+    const int tiles = P.tiles_m * P.tiles_n;
+    const int grid = std::min(tiles, kc::sm_count());
+    gemm_fp8_kernel<<<grid, kThreads, smem, stream>>>(P);
+    return kc::check_launch("gemm_fp8");
+}
+
+}  // extern "C"

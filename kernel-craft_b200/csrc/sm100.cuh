@@ -98,6 +98,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     }
 }
 
+// As mbar_wait, but cooperative with a CTA-wide abort flag in shared memory:
+// returns false at once when another thread already gave up, and raises the
+// flag itself on a timeout, so a broken pipeline unwinds in one timeout
+// instead of one per wait.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                   uint64_t timeout_ns = KC_WAIT_TIMEOUT_NS) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if (globaltimer() - t0 > timeout_ns) {
+            record_status(KC_ERR_TIMEOUT);
+            *abort = 1;
+            return false;
+        }
+    }
+}
+
 // --------------------------------------------------------- async copies ----
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes).
 // dst, src 16-byte aligned; bytes a multiple of 16.

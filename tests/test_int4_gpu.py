@@ -178,7 +178,7 @@ def test_w4a16_gemv_7b_shapes(cuda, K, N, M):
 
 def test_w4a16_grouped_matches_single(cuda):
     gs, M = 128, 4
-    shapes = [(4096, 1536), (4096, 512), (1024, 2752), (1376, 512)]   # (K, N)
+    shapes = [(4096, 1536), (4096, 512), (1024, 2752), (1408, 512)]   # (K, N), K % 128 == 0
     import kernel_craft_torch_ops as ops
     probs, singles = [], []
     for i, (K, N) in enumerate(shapes):

@@ -18,6 +18,7 @@ def test_bounded_wait_times_out_and_context_survives(cuda):
     waited = torch.full((1,), -7, dtype=torch.int32, device=cuda)
     kc_lib.check(l.kc_selftest_bounded_wait(200_000_000, ptr(waited), stream()))   # 0.2 s
     assert l.kc_get_device_status() == kc_lib.KC_ERR_TIMEOUT
+    assert l.kc_get_last_error() == kc_lib.KC_ERR_TIMEOUT      # also recorded on the thread
     assert 200 <= int(host(waited)[0]) < 5000
     assert l.kc_get_device_status() == kc_lib.KC_OK          # reading cleared it
     # the context is still usable: a real kernel runs and is correct

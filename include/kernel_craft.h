@@ -226,6 +226,19 @@ KC_API int kc_smoothquant_scale(const float* in, const float* smooth, float* out
 KC_API int kc_gemm_fp8(const int8_t* a_codes, const float* sa, const int8_t* w_codes, const float* sw,
                        void* out, int out_f32, int M, int N, int K, int ldc, cudaStream_t stream);
 
+/* W4A16 GEMM (prefill) on the tcgen05 tensor cores:
+ * out[m, n] = sum_k x[m, k] * w[n, k] with w[n, k] = bf16((u - 8) * s[n, k / gs]),
+ * the exact bf16 weights kc_dequantize_w4_bf16 produces (GPTQ symmetric INT4,
+ * the reference's dequantize_int4 of packed ^ 0x88 with zero points 0,
+ * quant_int4.cu:99-104), fp32 accumulation, written as bf16 (out_f32 = 0) or
+ * fp32 (out_f32 = 1) with row pitch ldc (elements).  x bf16 [M, K],
+ * packed u8 [N, K/2] (low nibble = even k), scales fp16 [N, K/gs].
+ * Requires K % 64 == 0, group_size % 64 == 0 dividing K, ldc >= N and
+ * 16-byte aligned x and packed. */
+KC_API int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
+                         void* out, int out_f32, int M, int N, int K, int group_size, int ldc,
+                         cudaStream_t stream);
+
 /* fp32 C[M,N] = A[M,K] * B[N,K]^T (the column/row-parallel shard GEMM). */
 KC_API int kc_sgemm_nt(const float* A, const float* B, float* C, int M, int N, int K,
                 cudaStream_t stream);

@@ -1,0 +1,329 @@
+// gemm_w4a16.cu -- W4A16 GEMM (prefill) on the 5th-generation tensor cores (sm_100a).
+//
+// C[m, n] = sum_k x[m, k] * w[n, k],  w[n, k] = bf16_rne((u - 8) * s[n, k / gs])
+// x bf16 [M, K] (K-major), packed u8 [N, K/2] (low nibble = even k), fp16 scales
+// [N, K/gs], fp32 accumulation, bf16 (or fp32) C [M, N].  The dequantized weights
+// are exactly the ones kc_dequantize_w4_bf16 produces (the reference dequant of
+// packed ^ 0x88 with zero points 0, quant_int4.cu:99-104, rounded to bf16).
+//
+// The weights are the MMA's A operand and live in TMEM, the activations are the
+// B operand in shared memory, so the accumulator holds C^T tiles
+// (128 weight rows x 256 tokens):
+//  * warp 0, TMA producer: per 64-k step a 256-token x 128-byte activation box
+//    (128-byte swizzle, K-major) and a 128-row x 32-byte packed-weight box, into
+//    a 4-stage ring;
+//  * warps 2-5, converters: thread i owns weight row i of the tile (= TMEM lane
+//    i); it turns its 64 nibbles into bf16 (u - 8) * s in fp32 with one RNE and
+//    writes them with tcgen05.st as 32 TMEM columns of a 4-stage A ring;
+//  * warp 1: allocates TMEM (256 accumulator + 4 x 32 A columns) and one lane
+//    issues tcgen05.mma kind::f16 (A from TMEM, B from shared memory; M 128,
+//    N 256, K 16) four times per step, committing to the stage barriers;
+//  * warps 6-9, epilogue: tcgen05.ld 32 token columns at a time, convert and
+//    store; the write of C[m, n] by the 32 lanes (consecutive n) is coalesced.
+// Staging bf16 weights in shared memory instead would need ~160 B/clk of
+// shared-memory bandwidth per SM at full MMA rate (above the ~128 B/clk
+// available); this layout needs ~100.  No TMA multicast is used.
+#include <algorithm>
+
+#include "kc_common.cuh"
+#include "sm100.cuh"
+#include "tensor_map.cuh"
+
+namespace {
+
+constexpr int BW = 128;      // weight rows per tile (MMA M)
+constexpr int BT = 256;      // tokens per tile (MMA N)
+constexpr int BK = 64;       // k per stage
+constexpr int kStages = 4;
+constexpr int kXBytes = BT * BK * 2;      // 32 KB activations per stage
+constexpr int kWBytes = BW * BK / 2;      // 4 KB packed weights per stage
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccCol = 0;           // accumulator columns [0, 256)
+constexpr uint32_t kACol = 256;           // A ring columns [256, 384)
+
+struct alignas(64) Params {
+    CUtensorMap xmap;   // activations bf16 {K, M}, box {64, 256}, 128-byte swizzle
+    CUtensorMap wmap;   // packed weights u8 {K/2, N}, box {32, 128}
+    const __half* scales;
+    void* out;
+    int M, N, K, gs, ldc, out_f32;
+    int tiles_w, tiles_t;
+    uint32_t magic;     // 0x3F800000 (1.0f), kept in a register
+};
+
+struct Smem {
+    uint8_t x[kStages][kXBytes];   // 1024-byte aligned (swizzle atoms)
+    uint8_t w[kStages][kWBytes];
+    uint64_t full[kStages];        // activations + packed weights landed (tx)
+    uint64_t empty[kStages];       // MMA (commit) and converters (4 warps) done with the stage
+    uint64_t afull[kStages];       // converters wrote the TMEM A stage
+    uint64_t aempty[kStages];      // MMA done reading the TMEM A stage (commit)
+    uint64_t dfull;                // accumulator complete (commit)
+    uint64_t dempty;               // epilogue drained the accumulator (4 warps)
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr));
+    return v;
+}
+
+// (x & mask) | magic in one LOP3 (magic passed in a register so the compiler
+// cannot fold it into a second immediate)
+template <uint32_t kMask>
+__device__ __forceinline__ float nib_float(uint32_t x, uint32_t magic) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(x), "n"(kMask), "r"(magic));
+    return __uint_as_float(r);
+}
+
+// Per-group constants of the exact dequantization.  A nibble u placed at bit p
+// (8, 12 or 16) of 1.0f reads f = 1 + u * 2^(p-23); then
+//   fma(f, s * 2^(23-p), -(2^(23-p) + 8) * s) = (u - 8) * s
+// exactly: s is an fp16 value (11 significant bits), so s * 2^(23-p) and
+// (2^(23-p) + 8) * s (at most 13 + 11 bits) are exact fp32 values, the fma
+// forms the exact sum, and (u - 8) * s (at most 15 bits) rounds to itself.
+// One rounding then remains, the RNE to bf16 -- the same value as
+// bf16_rne(float(u - 8) * s).
+struct GroupConst {
+    float m8, a8, m12, a12, m16, a16;
+    __device__ __forceinline__ explicit GroupConst(float s)
+        : m8(s * 32768.0f), a8(s * -32776.0f), m12(s * 2048.0f), a12(s * -2056.0f),
+          m16(s * 128.0f), a16(s * -136.0f) {}
+};
+
+// 8 nibbles of one packed word (k = 8i .. 8i+7, low nibble first) -> 4 bf16x2
+__device__ __forceinline__ void dequant_word(uint32_t w, const GroupConst& g, uint32_t magic,
+                                             uint32_t* out) {
+    const uint32_t lo = w << 8, hi = w >> 12;   // nibbles 0,1 -> bits 8,12; 5,6,7 -> 8,12,16
+    const float w0 = __fmaf_rn(nib_float<0x00000F00u>(lo, magic), g.m8, g.a8);
+    const float w1 = __fmaf_rn(nib_float<0x0000F000u>(lo, magic), g.m12, g.a12);
+    const float w2 = __fmaf_rn(nib_float<0x00000F00u>(w, magic), g.m8, g.a8);
+    const float w3 = __fmaf_rn(nib_float<0x0000F000u>(w, magic), g.m12, g.a12);
+    const float w4 = __fmaf_rn(nib_float<0x000F0000u>(w, magic), g.m16, g.a16);
+    const float w5 = __fmaf_rn(nib_float<0x00000F00u>(hi, magic), g.m8, g.a8);
+    const float w6 = __fmaf_rn(nib_float<0x0000F000u>(hi, magic), g.m12, g.a12);
+    const float w7 = __fmaf_rn(nib_float<0x000F0000u>(hi, magic), g.m16, g.a16);
+    out[0] = bf16x2_bits(w0, w1);
+    out[1] = bf16x2_bits(w2, w3);
+    out[2] = bf16x2_bits(w4, w5);
+    out[3] = bf16x2_bits(w6, w7);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_constant__ Params P) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = sm100::smem_u32(smem_raw);
+    Smem& S = *reinterpret_cast<Smem*>(smem_raw + (((raw + 1023u) & ~1023u) - raw));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles = P.tiles_w * P.tiles_t;
+    const int ksteps = P.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            sm100::mbar_init(&S.full[i], 1);
+            sm100::mbar_init(&S.empty[i], 1 + 4);
+            sm100::mbar_init(&S.afull[i], 4);
+            sm100::mbar_init(&S.aempty[i], 1);
+        }
+        sm100::mbar_init(&S.dfull, 1);
+        sm100::mbar_init(&S.dempty, 4);
+        sm100::mbar_init(&S.drain, 1);
+        S.abort = 0;
+        sm100::fence_barrier_init();
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(&S.tmem_base, kTmemCols);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = S.tmem_base;
+    volatile int* abort = &S.abort;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer -----------------------------
+        if (lane == 0) {
+            sm100::prefetch_tensormap(&P.xmap);
+            sm100::prefetch_tensormap(&P.wmap);
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+                const int n0 = (tile % P.tiles_w) * BW, m0 = (tile / P.tiles_w) * BT;
+                for (int ks = 0; ks < ksteps; ++ks, ++it) {
+                    const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+                    sm100::mbar_wait_or_abort(&S.empty[s], ph ^ 1u, abort);
+                    sm100::mbar_arrive_expect_tx(&S.full[s], kXBytes + kWBytes);
+                    sm100::tma_load_2d(S.x[s], &P.xmap, ks * BK, m0, &S.full[s]);
+                    sm100::tma_load_2d(S.w[s], &P.wmap, ks * (BK / 2), n0, &S.full[s]);
+                }
+            }
+            for (uint32_t j = it > (uint32_t)kStages ? it - kStages : 0u; j < it; ++j)
+                sm100::mbar_wait(&S.full[j % kStages], (j / kStages) & 1u, 200000000ull);
+        }
+    } else if (warp == 1) {
+        // ------------------------------- MMA issuer -------------------------------
+        if (lane == 0) {
+            const uint32_t idesc = sm100::umma_idesc(sm100::kFmtBF16, sm100::kFmtBF16, BW, BT);
+            uint32_t it = 0, t = 0;
+            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+                sm100::mbar_wait_or_abort(&S.dempty, (t & 1u) ^ 1u, abort);
+                sm100::tc_fence_after();
+                for (int ks = 0; ks < ksteps; ++ks, ++it) {
+                    const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+                    sm100::mbar_wait_or_abort(&S.full[s], ph, abort);
+                    sm100::mbar_wait_or_abort(&S.afull[s], ph, abort);
+                    sm100::tc_fence_after();
+                    const uint64_t bdesc = sm100::umma_desc_sw128(sm100::smem_u32(S.x[s]));
+                    const uint32_t a_tmem = tmem + kACol + s * (BK / 2);
+#pragma unroll
+                    for (int j = 0; j < BK / 16; ++j)  // K = 16 per instruction
+                        sm100::umma_f16_ts(tmem + kAccCol, a_tmem + j * 8, bdesc + 2 * j, idesc,
+                                           (ks | j) != 0 ? 1u : 0u);
+                    sm100::tc_commit(&S.empty[s]);   // activations free
+                    sm100::tc_commit(&S.aempty[s]);  // TMEM A stage free
+                }
+                sm100::tc_commit(&S.dfull);
+            }
+            sm100::tc_commit(&S.drain);
+            sm100::mbar_wait(&S.drain, 0, 200000000ull);
+        }
+    } else if (warp < 6) {
+        // -------------------------------- converters --------------------------------
+        const int q = warp & 3;                 // TMEM lane quarter
+        const int row = q * 32 + lane;          // weight row within the tile
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        uint32_t it = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            const int n0 = (tile % P.tiles_w) * BW;
+            const int n = min(n0 + row, P.N - 1);
+            const __half* srow = P.scales + (size_t)n * (P.K / P.gs);
+            float s_next = __half2float(srow[0]);
+            for (int ks = 0; ks < ksteps; ++ks, ++it) {
+                const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
+                const GroupConst gc(s_next);
+                if (ks + 1 < ksteps) s_next = __half2float(srow[((ks + 1) * BK) / P.gs]);
+                sm100::mbar_wait_or_abort(&S.full[s], ph, abort);
+                const uint32_t wa = sm100::smem_u32(S.w[s]) + row * (BK / 2);
+                const uint4 p0 = lds128(wa), p1 = lds128(wa + 16);
+                __syncwarp();
+                if (lane == 0) sm100::mbar_arrive(&S.empty[s]);  // packed bytes consumed
+                const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+                uint32_t v[32];  // column c of the A stage holds k = 2c (low half), 2c + 1
+#pragma unroll
+                for (int i = 0; i < 8; ++i) dequant_word(words[i], gc, P.magic, v + 4 * i);
+                sm100::mbar_wait_or_abort(&S.aempty[s], ph ^ 1u, abort);
+                __syncwarp();
+                sm100::tc_fence_after();
+                const uint32_t col = tmem + kACol + s * (BK / 2) + lane_addr;
+                uint32_t r0[16], r1[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) { r0[i] = v[i]; r1[i] = v[16 + i]; }
+                sm100::tmem_st_32x32b_x16(col, r0);
+                sm100::tmem_st_32x32b_x16(col + 16, r1);
+                sm100::tmem_wait_st();
+                sm100::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) sm100::mbar_arrive(&S.afull[s]);
+            }
+        }
+    } else {
+        // -------------------------------- epilogue --------------------------------
+        const int q = warp & 3;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        uint32_t t = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+            const int n0 = (tile % P.tiles_w) * BW, m0 = (tile / P.tiles_w) * BT;
+            const int n = n0 + q * 32 + lane;
+            sm100::mbar_wait_or_abort(&S.dfull, t & 1u, abort);
+            sm100::tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < BT / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                sm100::tmem_ld_32x32b_x32(tmem + kAccCol + lane_addr + c * 32, r);
+                sm100::tmem_wait_ld();
+                const int mb = m0 + c * 32;
+                if (n < P.N) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        if (mb + i < P.M) {
+                            const float f = __uint_as_float(r[i]);
+                            if (P.out_f32)
+                                reinterpret_cast<float*>(P.out)[(size_t)(mb + i) * P.ldc + n] = f;
+                            else
+                                reinterpret_cast<__nv_bfloat16*>(P.out)[(size_t)(mb + i) * P.ldc + n] =
+                                    __float2bfloat16_rn(f);
+                        }
+                    }
+                }
+            }
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&S.dempty);
+        }
+    }
+
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (warp == 1) sm100::tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace
+
+KC_DEFINE_STATUS_READER(gemm_w4a16)
+
+extern "C" {
+
+int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
+                  void* out, int out_f32, int M, int N, int K, int group_size, int ldc,
+                  cudaStream_t stream) {
+    KC_REQUIRE(x_bf16 && packed && scales_f16 && out, KC_ERR_INVALID_ARG, "null pointer argument");
+    KC_REQUIRE(M >= 0 && N >= 0 && K >= 0, KC_ERR_INVALID_ARG, "negative size");
+    if (M == 0 || N == 0) return KC_OK;
+    KC_REQUIRE(K > 0 && K % BK == 0, KC_ERR_INVALID_ARG, "K=%d must be a positive multiple of %d", K, BK);
+    KC_REQUIRE(group_size > 0 && group_size % BK == 0 && K % group_size == 0, KC_ERR_INVALID_ARG,
+               "group_size=%d must be a multiple of %d dividing K=%d", group_size, BK, K);
+    KC_REQUIRE(ldc >= N, KC_ERR_INVALID_ARG, "ldc=%d < N=%d", ldc, N);
+    KC_REQUIRE(kc::aligned(x_bf16, 16) && kc::aligned(packed, 16) && kc::aligned(scales_f16, 2) &&
+                   kc::aligned(out, 4),
+               KC_ERR_ALIGNMENT, "x and packed must be 16-byte aligned");
+    Params P{};
+    int st = kc::encode_2d(&P.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x_bf16, (uint64_t)K, (uint64_t)M,
+                           (uint64_t)K * 2, BK, BT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = kc::encode_2d(&P.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, (uint64_t)(K / 2), (uint64_t)N,
+                       (uint64_t)(K / 2), BK / 2, BW, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    P.scales = reinterpret_cast<const __half*>(scales_f16);
+    P.out = out;
+    P.M = M;
+    P.N = N;
+    P.K = K;
+    P.gs = group_size;
+    P.ldc = ldc;
+    P.out_f32 = out_f32 ? 1 : 0;
+    P.tiles_w = (N + BW - 1) / BW;
+    P.tiles_t = (M + BT - 1) / BT;
+    P.magic = 0x3F800000u;
+    const size_t smem = sizeof(Smem) + 1024;
+    KC_CUDA_TRY(cudaFuncSetAttribute(gemm_w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem),
+                "gemm_w4a16 shared-memory attribute");
+    const int tiles = P.tiles_w * P.tiles_t;
+    gemm_w4a16_kernel<<<std::min(tiles, kc::sm_count()), kThreads, smem, stream>>>(P);
+    return kc::check_launch("gemm_w4a16");
+}
+
+}  // extern "C"

@@ -87,6 +87,7 @@ _PROTOS = [
     ("kc_smoothquant_scale", ci, [vp, vp, vp, ci, ci, vp]),
     ("kc_sgemm_nt", ci, [vp, vp, vp, ci, ci, ci, vp]),
     ("kc_gemm_fp8", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
+    ("kc_gemm_w4a16", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_nccl_unique_id_bytes", ci, []),
     ("kc_nccl_get_unique_id", ci, [vp]),
     ("kc_nccl_comm_init_rank", ci, [vp, ci, vp, ci]),

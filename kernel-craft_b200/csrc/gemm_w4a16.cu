@@ -12,17 +12,24 @@
 //  * warp 0, TMA producer: per 64-k step a 256-token x 128-byte activation box
 //    (128-byte swizzle, K-major) and a 128-row x 32-byte packed-weight box, into
 //    a 4-stage ring;
-//  * warps 2-5, converters: thread i owns weight row i of the tile (= TMEM lane
-//    i); it turns its 64 nibbles into bf16 (u - 8) * s in fp32 with one RNE and
-//    writes them with tcgen05.st as 32 TMEM columns of a 4-stage A ring;
+//  * warps 2-9, converters, two per TMEM lane quarter taking alternate steps:
+//    thread i of a quarter owns weight row i (= TMEM lane i); it turns its 64
+//    nibbles into bf16 (u - 8) * s with one exact fma and one RNE and writes
+//    them with tcgen05.st as 32 TMEM columns of a 4-stage A ring.  Two warps
+//    per quarter overlap one warp's TMEM-store wait with the other's ALU work;
 //  * warp 1: allocates TMEM (256 accumulator + 4 x 32 A columns) and one lane
 //    issues tcgen05.mma kind::f16 (A from TMEM, B from shared memory; M 128,
 //    N 256, K 16) four times per step, committing to the stage barriers;
-//  * warps 6-9, epilogue: tcgen05.ld 32 token columns at a time, convert and
-//    store; the write of C[m, n] by the 32 lanes (consecutive n) is coalesced.
-// Staging bf16 weights in shared memory instead would need ~160 B/clk of
-// shared-memory bandwidth per SM at full MMA rate (above the ~128 B/clk
-// available); this layout needs ~100.  No TMA multicast is used.
+//  * warps 10-13, epilogue: drain the accumulator with tcgen05.ld, release it to
+//    the MMA as soon as the last load returns, convert to bf16 into a
+//    shared-memory tile and write it with a TMA store that runs under the next
+//    tile's main loop (fp32 output, or a pitch the TMA cannot address, falls
+//    back to direct coalesced stores).
+// TMEM holds one accumulator only (256 + 128 A columns of 512), so the early
+// release keeps the MMA idle per tile to the drain time.  Staging bf16 weights
+// in shared memory instead would need ~160 B/clk of shared-memory bandwidth per
+// SM at full MMA rate (above the ~128 B/clk available); this layout needs
+// ~100.  No TMA multicast is used.
 #include <algorithm>
 
 #include "kc_common.cuh"
@@ -37,7 +44,10 @@ constexpr int BK = 64;       // k per stage
 constexpr int kStages = 4;
 constexpr int kXBytes = BT * BK * 2;      // 32 KB activations per stage
 constexpr int kWBytes = BW * BK / 2;      // 4 KB packed weights per stage
-constexpr int kThreads = 320;
+constexpr int kConvWarps = 8;
+constexpr int kEpiWarp0 = 2 + kConvWarps;            // warps 10..13
+constexpr int kThreads = (kEpiWarp0 + 4) * 32;       // 448
+constexpr int kStageBytes = BT * 32 * 2;             // 16 KB bf16 staging per epilogue warp
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCol = 0;           // accumulator columns [0, 256)
 constexpr uint32_t kACol = 256;           // A ring columns [256, 384)
@@ -45,9 +55,10 @@ constexpr uint32_t kACol = 256;           // A ring columns [256, 384)
 struct alignas(64) Params {
     CUtensorMap xmap;   // activations bf16 {K, M}, box {64, 256}, 128-byte swizzle
     CUtensorMap wmap;   // packed weights u8 {K/2, N}, box {32, 128}
+    CUtensorMap omap;   // output bf16 {N, M} (pitch ldc), box {32, 256}; valid if tma_out
     const __half* scales;
     void* out;
-    int M, N, K, gs, ldc, out_f32;
+    int M, N, K, gs, ldc, out_f32, tma_out;
     int tiles_w, tiles_t;
     uint32_t magic;     // 0x3F800000 (1.0f), kept in a register
 };
@@ -55,8 +66,9 @@ struct alignas(64) Params {
 struct Smem {
     uint8_t x[kStages][kXBytes];   // 1024-byte aligned (swizzle atoms)
     uint8_t w[kStages][kWBytes];
+    uint8_t stage[4][kStageBytes]; // epilogue tiles: [256 tokens][32 weight rows] bf16
     uint64_t full[kStages];        // activations + packed weights landed (tx)
-    uint64_t empty[kStages];       // MMA (commit) and converters (4 warps) done with the stage
+    uint64_t empty[kStages];       // MMA (commit) and the stage's 4 converter warps done
     uint64_t afull[kStages];       // converters wrote the TMEM A stage
     uint64_t aempty[kStages];      // MMA done reading the TMEM A stage (commit)
     uint64_t dfull;                // accumulator complete (commit)
@@ -198,9 +210,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
             sm100::tc_commit(&S.drain);
             sm100::mbar_wait(&S.drain, 0, 200000000ull);
         }
-    } else if (warp < 6) {
+    } else if (warp < kEpiWarp0) {
         // -------------------------------- converters --------------------------------
-        const int q = warp & 3;                 // TMEM lane quarter
+        const int q = warp & 3;                 // TMEM lane quarter (warp % 4 rule)
+        const uint32_t par = (uint32_t)(warp - 2) >> 2;  // this warp takes steps it % 2 == par
         const int row = q * 32 + lane;          // weight row within the tile
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         uint32_t it = 0;
@@ -208,11 +221,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
             const int n0 = (tile % P.tiles_w) * BW;
             const int n = min(n0 + row, P.N - 1);
             const __half* srow = P.scales + (size_t)n * (P.K / P.gs);
-            float s_next = __half2float(srow[0]);
             for (int ks = 0; ks < ksteps; ++ks, ++it) {
+                if ((it & 1u) != par) continue;
                 const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
-                const GroupConst gc(s_next);
-                if (ks + 1 < ksteps) s_next = __half2float(srow[((ks + 1) * BK) / P.gs]);
+                const GroupConst gc(__half2float(__ldg(srow + (ks * BK) / P.gs)));
                 sm100::mbar_wait_or_abort(&S.full[s], ph, abort);
                 const uint32_t wa = sm100::smem_u32(S.w[s]) + row * (BK / 2);
                 const uint4 p0 = lds128(wa), p1 = lds128(wa + 16);
@@ -241,37 +253,70 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
         // -------------------------------- epilogue --------------------------------
         const int q = warp & 3;
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        uint8_t* stage = S.stage[q];
         uint32_t t = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
             const int n0 = (tile % P.tiles_w) * BW, m0 = (tile / P.tiles_w) * BT;
             const int n = n0 + q * 32 + lane;
             sm100::mbar_wait_or_abort(&S.dfull, t & 1u, abort);
             sm100::tc_fence_after();
-#pragma unroll 1
-            for (int c = 0; c < BT / 32; ++c) {
-                uint32_t r[32];
+            if (P.tma_out) {
+                // the previous tile's TMA store has finished reading the staging tile
+                if (lane == 0) sm100::bulk_wait_group_read0();
                 __syncwarp();
-                sm100::tmem_ld_32x32b_x32(tmem + kAccCol + lane_addr + c * 32, r);
-                sm100::tmem_wait_ld();
-                const int mb = m0 + c * 32;
-                if (n < P.N) {
+#pragma unroll 1
+                for (int c = 0; c < BT / 64; ++c) {
+                    uint32_t r[32], r2[32];
+                    __syncwarp();
+                    sm100::tmem_ld_32x32b_x32(tmem + kAccCol + lane_addr + c * 64, r);
+                    sm100::tmem_ld_32x32b_x32(tmem + kAccCol + lane_addr + c * 64 + 32, r2);
+                    sm100::tmem_wait_ld();
+                    if (c == BT / 64 - 1) {  // accumulator drained: hand it back to the MMA
+                        sm100::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) sm100::mbar_arrive(&S.dempty);
+                    }
+                    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + c * 64 * 32 + lane;
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        if (mb + i < P.M) {
-                            const float f = __uint_as_float(r[i]);
-                            if (P.out_f32)
-                                reinterpret_cast<float*>(P.out)[(size_t)(mb + i) * P.ldc + n] = f;
-                            else
-                                reinterpret_cast<__nv_bfloat16*>(P.out)[(size_t)(mb + i) * P.ldc + n] =
-                                    __float2bfloat16_rn(f);
+                        o[i * 32] = __float2bfloat16_rn(__uint_as_float(r[i]));
+                        o[(32 + i) * 32] = __float2bfloat16_rn(__uint_as_float(r2[i]));
+                    }
+                }
+                sm100::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && n0 + q * 32 < P.N) {
+                    sm100::tma_store_2d(&P.omap, stage, n0 + q * 32, m0);
+                    sm100::bulk_commit_group();
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BT / 32; ++c) {
+                    uint32_t r[32];
+                    __syncwarp();
+                    sm100::tmem_ld_32x32b_x32(tmem + kAccCol + lane_addr + c * 32, r);
+                    sm100::tmem_wait_ld();
+                    const int mb = m0 + c * 32;
+                    if (n < P.N) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (mb + i < P.M) {
+                                const float f = __uint_as_float(r[i]);
+                                if (P.out_f32)
+                                    reinterpret_cast<float*>(P.out)[(size_t)(mb + i) * P.ldc + n] = f;
+                                else
+                                    reinterpret_cast<__nv_bfloat16*>(P.out)[(size_t)(mb + i) * P.ldc + n] =
+                                        __float2bfloat16_rn(f);
+                            }
                         }
                     }
                 }
+                sm100::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) sm100::mbar_arrive(&S.dempty);
             }
-            sm100::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) sm100::mbar_arrive(&S.dempty);
         }
+        if (lane == 0) sm100::bulk_wait_group0();  // stores complete before the CTA exits
     }
 
     sm100::tc_fence_before();
@@ -306,6 +351,12 @@ int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t*
     st = kc::encode_2d(&P.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, (uint64_t)(K / 2), (uint64_t)N,
                        (uint64_t)(K / 2), BK / 2, BW, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
+    P.tma_out = (!out_f32 && kc::aligned(out, 16) && ldc % 8 == 0) ? 1 : 0;
+    if (P.tma_out) {
+        st = kc::encode_2d(&P.omap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, (uint64_t)N, (uint64_t)M,
+                           (uint64_t)ldc * 2, 32, BT, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    }
     P.scales = reinterpret_cast<const __half*>(scales_f16);
     P.out = out;
     P.M = M;

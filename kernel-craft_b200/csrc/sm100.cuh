@@ -139,6 +139,32 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
+// 2-D tiled tensor copy shared -> global, tracked by the issuing thread's bulk
+// groups.  x >= 0 and y >= 0 (a store never starts at a negative coordinate);
+// x a multiple of 16 bytes; the part of the box outside the tensor is clipped.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map),
+                 "r"(x), "r"(y), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until every committed bulk group of this thread has finished reading
+// shared memory (the source may be overwritten) ...
+__device__ __forceinline__ void bulk_wait_group_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// ... or has completed entirely (writes visible in global memory).
+__device__ __forceinline__ void bulk_wait_group0() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) reads of them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

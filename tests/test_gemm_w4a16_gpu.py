@@ -36,7 +36,7 @@ def _exact_weight_ref(x_bits, packed, scales, N, K, gs):
 
 @pytest.mark.parametrize("M,N,K,gs", [(1, 128, 64, 64), (256, 256, 512, 128), (300, 200, 1024, 128),
                                       (513, 384, 2048, 64), (128, 1000, 4096, 128),
-                                      (257, 136, 256, 256)])
+                                      (257, 136, 256, 256), (64, 130, 128, 128)])
 def test_w4a16_gemm_small(cuda, M, N, K, gs):
     packed, scales = O.make_w4_gptq(N, K, gs, seed=M + N)
     x = O.make_activations_bf16(M, K, seed=K)

@@ -205,6 +205,24 @@ KC_API int kc_quantize_fp8_per_tensor(const float* in, int8_t* out, const float*
 KC_API int kc_quantize_fp8_per_tensor_dynamic(const float* in, int8_t* out, float* scale_out,
                                               long count, void* workspace, size_t workspace_bytes,
                                               cudaStream_t stream);
+/* The same quantization (identical codes and scale) for callers that may not
+ * allocate device memory at all -- code running under a caller-owned memory
+ * budget, an allocator-free serving loop, or a host binding with no device
+ * allocator to hand a workspace from.  No counterpart in the reference; it
+ * allocates nothing: its 256 KiB of scratch is a static array inside the
+ * library's own device image.  Limits and rules:
+ *  - count <= 2^30 elements; larger counts return KC_ERR_INVALID_ARG (use the
+ *    workspace variant above);
+ *  - the first call on each device (with that device current) looks up the
+ *    scratch address with cudaGetSymbolAddress; make that first call before
+ *    capturing any stream;
+ *  - one arrival counter in the scratch must read zero when a call starts: it
+ *    is zero when the library loads and every completed call leaves it at zero;
+ *  - calls that overlap on one device (different streams, threads or processes
+ *    sharing a context) share the scratch and race; serialize them. */
+KC_API int kc_quantize_fp8_per_tensor_dynamic_noalloc(const float* in, int8_t* out,
+                                                      float* scale_out, long count,
+                                                      cudaStream_t stream);
 /* SmoothQuant divide fused into per-token quantization: bit-identical to
  * launch_smoothquant_scale followed by launch_quantize_fp8(per_token=true),
  * without the fp32 round trip through HBM. */

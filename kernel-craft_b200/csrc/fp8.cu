@@ -12,6 +12,9 @@
 // from registers (the reference reads the row twice and stores bytes).
 #include <cuda_fp8.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "kc_common.cuh"
 
 namespace {
@@ -237,6 +240,82 @@ __global__ void smooth_scalar(const float* __restrict__ in, const float* __restr
         out[i] = __fdiv_rn(in[i], s[i % cols]);
 }
 
+// ---- allocation-free dynamic per-tensor quantization ---------------------------
+// Scratch lives in this module's own device memory instead of a caller buffer:
+// word 0 is an arrival counter, word 1 receives the tensor amax, words
+// 64.. hold one partial amax per CTA of the amax pass.  The counter is zero
+// when the module loads and every completed call leaves it at zero again; the
+// other words are fully rewritten by every call.
+constexpr long kNoAllocChunk = 16384;         // elements per CTA of the amax pass
+constexpr int kNoAllocMaxPartials = 65536;    // CTAs of the amax pass
+constexpr long kNoAllocMaxCount = kNoAllocChunk * kNoAllocMaxPartials;  // 2^30 elements
+constexpr int kNoAllocPartialBase = 64;
+static __device__ __align__(256) unsigned int g_fp8_noalloc_scratch[kNoAllocPartialBase + kNoAllocMaxPartials];
+
+// CTA b reduces elements [b * chunk, (b + 1) * chunk) to a partial amax; the
+// CTA that arrives last reduces the partials, publishes the amax in word 1 and
+// returns the counter to zero.
+__global__ void __launch_bounds__(256) amax_chunks_last_cta(const float* __restrict__ in, long n,
+                                                            unsigned int* scratch) {
+    __shared__ float red[32];
+    __shared__ int is_last;
+    const long base = blockIdx.x * kNoAllocChunk;
+    const long end = min(n, base + kNoAllocChunk);
+    float m = 0.0f;
+    long tail = base;
+    if (kc::aligned(in, 16)) {
+        const float4* in4 = reinterpret_cast<const float4*>(in);
+        for (long i = base / 4 + threadIdx.x; i < end / 4; i += blockDim.x) m = amax4(m, __ldcs(in4 + i));
+        tail = max(base, (end / 4) * 4);
+    }
+    for (long i = tail + threadIdx.x; i < end; i += blockDim.x) m = fmaxf(m, fabsf(in[i]));
+    m = block_max(m, red);
+    if (threadIdx.x == 0) {
+        scratch[kNoAllocPartialBase + blockIdx.x] = __float_as_uint(m);
+        __threadfence();
+        is_last = (atomicAdd(&scratch[0], 1u) == gridDim.x - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    float t = 0.0f;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x)
+        t = fmaxf(t, __uint_as_float(__ldcg(&scratch[kNoAllocPartialBase + i])));
+    t = block_max(t, red);
+    if (threadIdx.x == 0) {
+        scratch[1] = __float_as_uint(t);
+        scratch[0] = 0u;
+    }
+}
+
+// Device address of g_fp8_noalloc_scratch on the current device, looked up once
+// per device (cudaGetSymbolAddress) and cached.
+constexpr int kNoAllocMaxDevices = 64;
+std::atomic<unsigned int*> g_noalloc_scratch_ptr[kNoAllocMaxDevices];
+std::mutex g_noalloc_setup_mutex;
+
+int noalloc_scratch(unsigned int** out) {
+    int dev = 0;
+    KC_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    KC_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, KC_ERR_INVALID_ARG,
+               "device %d beyond the %d devices the no-alloc scratch table covers", dev,
+               kNoAllocMaxDevices);
+    unsigned int* p = g_noalloc_scratch_ptr[dev].load(std::memory_order_acquire);
+    if (p == nullptr) {
+        std::lock_guard<std::mutex> lock(g_noalloc_setup_mutex);
+        p = g_noalloc_scratch_ptr[dev].load(std::memory_order_relaxed);
+        if (p == nullptr) {
+            void* sym = nullptr;
+            KC_CUDA_TRY(cudaGetSymbolAddress(&sym, g_fp8_noalloc_scratch),
+                        "cudaGetSymbolAddress(no-alloc scratch)");
+            p = static_cast<unsigned int*>(sym);
+            g_noalloc_scratch_ptr[dev].store(p, std::memory_order_release);
+        }
+    }
+    *out = p;
+    return KC_OK;
+}
+
 int grid_1d(long items, int threads) {
     long g = (items + threads - 1) / threads;
     const long cap = (long)kc::sm_count() * (2048 / threads) * 4;
@@ -327,6 +406,25 @@ int kc_quantize_fp8_per_tensor_dynamic(const float* in, int8_t* out, float* scal
     quant_tensor_from_amax<<<grid_1d((count + 3) / 4, 256), 256, 0, stream>>>(in, out, count,
                                                                               amax_bits, scale_out);
     return kc::check_launch("quant_tensor_from_amax");
+}
+
+int kc_quantize_fp8_per_tensor_dynamic_noalloc(const float* in, int8_t* out, float* scale_out,
+                                               long count, cudaStream_t stream) {
+    KC_REQUIRE(in && out && scale_out, KC_ERR_INVALID_ARG, "null pointer argument");
+    KC_REQUIRE(count >= 0, KC_ERR_INVALID_ARG, "negative count");
+    KC_REQUIRE(count <= kNoAllocMaxCount, KC_ERR_INVALID_ARG,
+               "count %ld exceeds the no-alloc maximum of %ld elements (%d partials of %ld); use "
+               "kc_quantize_fp8_per_tensor_dynamic with a workspace",
+               count, kNoAllocMaxCount, kNoAllocMaxPartials, kNoAllocChunk);
+    unsigned int* scratch = nullptr;
+    const int st = noalloc_scratch(&scratch);
+    if (st != KC_OK) return st;
+    const int ctas = count > 0 ? kc::ceil_div(count, kNoAllocChunk) : 1;
+    amax_chunks_last_cta<<<ctas, 256, 0, stream>>>(in, count, scratch);
+    KC_CUDA_TRY(cudaGetLastError(), "amax_chunks_last_cta");
+    quant_tensor_from_amax<<<grid_1d((count + 3) / 4, 256), 256, 0, stream>>>(in, out, count,
+                                                                              scratch + 1, scale_out);
+    return kc::check_launch("quant_tensor_from_amax (no-alloc)");
 }
 
 int kc_dequantize_fp8(const int8_t* in, const float* scales, float* out, int rows, int cols,

@@ -82,6 +82,7 @@ _PROTOS = [
     ("kc_quantize_fp8_per_channel", ci, [vp, vp, vp, ci, ci, vp]),
     ("kc_quantize_fp8_per_tensor", ci, [vp, vp, vp, cl, vp]),
     ("kc_quantize_fp8_per_tensor_dynamic", ci, [vp, vp, vp, cl, vp, ctypes.c_size_t, vp]),
+    ("kc_quantize_fp8_per_tensor_dynamic_noalloc", ci, [vp, vp, vp, cl, vp]),
     ("kc_smoothquant_quantize_fp8", ci, [vp, vp, vp, vp, ci, ci, vp]),
     ("kc_dequantize_fp8", ci, [vp, vp, vp, ci, ci, cb, vp]),
     ("kc_smoothquant_scale", ci, [vp, vp, vp, ci, ci, vp]),

@@ -99,12 +99,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
         if (lane == 0) {
             sm100::prefetch_tensormap(&P.amap);
             sm100::prefetch_tensormap(&P.wmap);
-            uint32_t it = 0;
-            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+            uint32_t it = 0;   // loads issued; nothing more is issued after a failed wait
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
                 const int m0 = (tile % P.tiles_m) * BM, n0 = (tile / P.tiles_m) * BN;
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
-                    sm100::mbar_wait_or_abort(&S.empty[s], ph ^ 1u, abort);
+                    if (!(ok = sm100::mbar_wait_or_abort(&S.empty[s], ph ^ 1u, abort))) break;
                     sm100::mbar_arrive_expect_tx(&S.full[s], kABytes + kBBytes);
                     sm100::tma_load_2d(S.a[s], &P.amap, kb * BK, m0, &S.full[s]);
                     sm100::tma_load_2d(S.b[s], &P.wmap, kb * BK, n0, &S.full[s]);

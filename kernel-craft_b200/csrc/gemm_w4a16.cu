@@ -61,6 +61,7 @@ struct alignas(64) Params {
     int M, N, K, gs, ldc, out_f32, tma_out;
     int tiles_w, tiles_t;
     uint32_t magic;     // 0x3F800000 (1.0f), kept in a register
+    uint32_t gs_recip;      // ceil(2^32 / gs): k / gs == umulhi(k, gs_recip) for k * gs < 2^32
 };
 
 struct Smem {
@@ -169,12 +170,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
         if (lane == 0) {
             sm100::prefetch_tensormap(&P.xmap);
             sm100::prefetch_tensormap(&P.wmap);
-            uint32_t it = 0;
-            for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-                const int n0 = (tile % P.tiles_w) * BW, m0 = (tile / P.tiles_w) * BT;
+            uint32_t it = 0;   // loads issued; nothing more is issued after a failed wait
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+                const int n0 = (tile / P.tiles_t) * BW, m0 = (tile % P.tiles_t) * BT;
                 for (int ks = 0; ks < ksteps; ++ks, ++it) {
                     const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
-                    sm100::mbar_wait_or_abort(&S.empty[s], ph ^ 1u, abort);
+                    if (!(ok = sm100::mbar_wait_or_abort(&S.empty[s], ph ^ 1u, abort))) break;
                     sm100::mbar_arrive_expect_tx(&S.full[s], kXBytes + kWBytes);
                     sm100::tma_load_2d(S.x[s], &P.xmap, ks * BK, m0, &S.full[s]);
                     sm100::tma_load_2d(S.w[s], &P.wmap, ks * (BK / 2), n0, &S.full[s]);
@@ -218,13 +220,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         uint32_t it = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-            const int n0 = (tile % P.tiles_w) * BW;
+            const int n0 = (tile / P.tiles_t) * BW;
             const int n = min(n0 + row, P.N - 1);
             const __half* srow = P.scales + (size_t)n * (P.K / P.gs);
             for (int ks = 0; ks < ksteps; ++ks, ++it) {
                 if ((it & 1u) != par) continue;
                 const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
-                const GroupConst gc(__half2float(__ldg(srow + (ks * BK) / P.gs)));
+                const GroupConst gc(__half2float(__ldg(srow + __umulhi((uint32_t)(ks * BK), P.gs_recip))));
                 sm100::mbar_wait_or_abort(&S.full[s], ph, abort);
                 const uint32_t wa = sm100::smem_u32(S.w[s]) + row * (BK / 2);
                 const uint4 p0 = lds128(wa), p1 = lds128(wa + 16);
@@ -256,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
         uint8_t* stage = S.stage[q];
         uint32_t t = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
-            const int n0 = (tile % P.tiles_w) * BW, m0 = (tile / P.tiles_w) * BT;
+            const int n0 = (tile / P.tiles_t) * BW, m0 = (tile % P.tiles_t) * BT;
             const int n = n0 + q * 32 + lane;
             sm100::mbar_wait_or_abort(&S.dfull, t & 1u, abort);
             sm100::tc_fence_after();
@@ -341,6 +343,8 @@ int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t*
     KC_REQUIRE(group_size > 0 && group_size % BK == 0 && K % group_size == 0, KC_ERR_INVALID_ARG,
                "group_size=%d must be a multiple of %d dividing K=%d", group_size, BK, K);
     KC_REQUIRE(ldc >= N, KC_ERR_INVALID_ARG, "ldc=%d < N=%d", ldc, N);
+    KC_REQUIRE((uint64_t)K * (uint64_t)group_size < (1ull << 32), KC_ERR_INVALID_ARG,
+               "K * group_size must be below 2^32");
     KC_REQUIRE(kc::aligned(x_bf16, 16) && kc::aligned(packed, 16) && kc::aligned(scales_f16, 2) &&
                    kc::aligned(out, 4),
                KC_ERR_ALIGNMENT, "x and packed must be 16-byte aligned");
@@ -368,6 +372,7 @@ int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t*
     P.tiles_w = (N + BW - 1) / BW;
     P.tiles_t = (M + BT - 1) / BT;
     P.magic = 0x3F800000u;
+    P.gs_recip = (uint32_t)((0x100000000ull + (uint64_t)group_size - 1) / (uint64_t)group_size);
     const size_t smem = sizeof(Smem) + 1024;
     KC_CUDA_TRY(cudaFuncSetAttribute(gemm_w4a16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem),

@@ -10,26 +10,27 @@
 // contiguous runs of 128-k chunks (16 rows x 64 bytes = 1 KB each) and reduce
 // their partial sums through shared memory at the end of the tile.
 //
-// Memory pipeline: every warp owns a 6-stage ring in shared memory.  Its lane
-// 0 issues one 2-D TMA load per chunk (box 64 bytes x 16 rows of the packed
-// weight matrix; rows past N read as zero) onto the stage's mbarrier, running
-// five chunks ahead of the warp's compute, across tile boundaries; a tile's
-// fp16 scale block (16 contiguous rows) arrives by one bulk copy per tile,
-// issued a tile ahead.  So weights stream at full rate without holding
-// registers, and the compute loop never waits on a global load.
+// Memory pipeline: every warp owns a ring of kRing stages in shared memory,
+// each holding up to four chunks ("a quad", 4 KB).  Its lane 0 issues the
+// quad's 2-D TMA loads (box 64 bytes x 16 rows; rows past N read as zero) on
+// the stage's mbarrier, running kRing quads ahead of the warp's compute,
+// across tile boundaries; a tile's fp16 scale block (16 contiguous rows)
+// arrives by one bulk copy per tile, issued a tile ahead.  One wait and one
+// issue per 4 KB keeps the per-chunk bookkeeping small.
 //
 // Compute: a lane (g = lane / 4, t = lane % 4) reads rows g and g + 8, 16
-// bytes each, of the chunk and turns every 32-bit word into four bf16x2 MMA
+// bytes each, of a chunk and turns every 32-bit word into four bf16x2 MMA
 // fragments holding 128 + u exactly (nibble OR-ed into the mantissa of bf16
 // 128.0; 3 shifts + 4 LOP3 per 8 weights), fed straight from registers into
-// mma.sync m16n8k16 (weights as A, activations as B).  A second MMA with the
-// constant fragment -136 on the same activations turns the sum into
-// sum (u - 8) x without a per-weight subtraction; the group scale multiplies
-// the per-chunk fp32 partial product.  Activations are staged once per
-// problem in shared memory in fragment order (k0 k4 k1 k5 k2 k6 k3 k7 per
-// 8-block) when they fit, else read from global memory (L1-resident) and
-// permuted with PRMT.  MMA columns m >= M read a valid (clamped) activation
-// row and are discarded, so no lane predication is needed.
+// mma.sync m16n8k16 (weights as A, activations as B).  Activations are
+// staged once per problem in shared memory in fragment order (k0 k4 k1 k5 k2
+// k6 k3 k7 per 8-block) when they fit, together with their per-chunk sums, and
+// the offset is removed per chunk as sum (u - 8) x = sum (128 + u) x -
+// 136 * sum x; otherwise they are read from global memory (L1-resident),
+// permuted with PRMT, and a second MMA with the constant fragment -136 removes
+// the offset.  The group scale multiplies the per-chunk result.  MMA columns
+// m >= M read a valid (clamped) activation row and are
+// discarded, so no lane predication is needed.
 //
 // Dequantized weights never touch shared memory or TMEM: at M <= 16 the
 // kernel is bound by HBM, and staging bf16 weights for a tcgen05 A operand
@@ -61,24 +62,28 @@ struct alignas(64) Params {
     int gs;
     int gshift;      // group of 128-k chunk c is c >> gshift
     int xs_row;      // row pitch (elements) of the staged activations, 0 = not staged
+    int sx_chunks;   // chunk capacity of the staged activation sums
     uint32_t magic;  // 0x43004300 = bf16x2 (128, 128), held in a register (see nib_or)
-    uint32_t neg136; // 0xC308C308 = bf16x2 (-136, -136): the correction MMA's A fragment
+    uint32_t neg136; // 0xC308C308 = bf16x2 (-136, -136): the unstaged path's offset MMA fragment
 };
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kChunkBytes = 1024;                 // 16 rows x 64 bytes = 128 k
-constexpr int kRing = 4;                          // stages per warp, each a pair of chunks
+constexpr int kQuad = 4;                          // chunks per stage
+constexpr int kRing = 2;                          // stages per warp
 constexpr int kScaleHalves = 16 * 128;            // 16 rows x up to 128 groups
+constexpr int kSxCols = 16;                       // activation-sum columns (M padded)
 
 template <int NT>
 struct Smem {
-    uint8_t ring[kWarps][kRing][2][kChunkBytes];  // TMA destinations, 1024-byte aligned
+    uint8_t ring[kWarps][kRing][kQuad][kChunkBytes];  // TMA destinations, 1024-byte aligned
     __half scales[2][kScaleHalves];
     float red[kWarps][16][NT * 8 + 1];
     uint64_t wfull[kWarps][kRing];
     uint64_t sfull[2];
-    // staged activations (bf16, fragment order) follow, 16-byte aligned
+    // then, if staged: the activation sums float[sx_chunks][kSxCols] and the
+    // activations (bf16, fragment order), 16-byte aligned
 };
 
 template <int NT>
@@ -91,6 +96,12 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ float2 lds_f2(uint32_t addr) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
     return v;
 }
 
@@ -140,53 +151,56 @@ __device__ __forceinline__ int problem_index(const Params& P, int tile) {
     return pi;
 }
 
-// Pair range [begin, end) of warp w for a row of C 128-k chunks (ceil(C/2) pairs).
-__device__ __forceinline__ void warp_pairs(int C, int w, int& begin, int& end) {
-    const int pairs = (C + 1) >> 1;
-    begin = (w * pairs) >> 3;
-    end = ((w + 1) * pairs) >> 3;
+// Chunk range [begin, end) of warp w for a row of C 128-k chunks.
+__device__ __forceinline__ void warp_chunks(int C, int w, int& begin, int& end) {
+    begin = (w * C) >> 3;
+    end = ((w + 1) * C) >> 3;
 }
 
-// A warp's position in its own sequence of (tile, chunk pair) work items.
+// A warp's position in its own sequence of (tile, quad) work items.
 struct Cursor {
-    int tile, pr, pend, pi, chunks;
+    int tile, c, cend, pi;
 };
 
 __device__ __forceinline__ void cursor_settle(const Params& P, Cursor& cu, int warp) {
-    while (cu.tile < P.total_tiles && cu.pr >= cu.pend) {
+    while (cu.tile < P.total_tiles && cu.c >= cu.cend) {
         cu.tile += gridDim.x;
         if (cu.tile >= P.total_tiles) break;
         cu.pi = problem_index(P, cu.tile);
-        cu.chunks = P.p[cu.pi].K >> 7;
-        warp_pairs(cu.chunks, warp, cu.pr, cu.pend);
+        warp_chunks(P.p[cu.pi].K >> 7, warp, cu.c, cu.cend);
     }
 }
 
 // The whole warp steps the (warp-uniform) cursor; the arm of the stage's
-// mbarrier and the TMA loads of the pair (one or two 1 KB boxes) are issued by
+// mbarrier and the quad's TMA loads (one 1 KB box per chunk) are issued by
 // lane 0 through predicated PTX, so no divergent branch is taken.
-__device__ __forceinline__ void issue_pair(const Params& P, Cursor& cu, uint32_t dst, uint32_t bar,
+__device__ __forceinline__ void issue_quad(const Params& P, Cursor& cu, uint32_t dst, uint32_t bar,
                                            int warp, bool leader) {
     if (cu.tile >= P.total_tiles) return;
-    const Prob& pr = P.p[cu.pi];
-    const int row0 = (cu.tile - pr.tile_begin) * 16;
-    const int c0 = 2 * cu.pr;
-    const int two = (c0 + 1 < cu.chunks) ? 1 : 0;
-    const uint32_t bytes = two ? 2 * kChunkBytes : kChunkBytes;
+    const int row0 = (cu.tile - P.p[cu.pi].tile_begin) * 16;
+    const int n = min(kQuad, cu.cend - cu.c);
     const CUtensorMap* map = &P.wmap[cu.pi];
+    const int x0 = cu.c * 64;
     asm volatile(
-        "{\n\t.reg .pred l, l2;\n\t"
+        "{\n\t.reg .pred l, l1, l2, l3;\n\t"
         "setp.ne.b32 l, %0, 0;\n\t"
-        "setp.ne.and.b32 l2, %6, 0, l;\n\t"
+        "setp.gt.and.s32 l1, %6, 1, l;\n\t"
+        "setp.gt.and.s32 l2, %6, 2, l;\n\t"
+        "setp.gt.and.s32 l3, %6, 3, l;\n\t"
         "@l mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n\t"
         "@l cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
         " [%3], [%4, {%5, %7}], [%1];\n\t"
+        "@l1 cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%8], [%4, {%9, %7}], [%1];\n\t"
         "@l2 cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-        " [%8], [%4, {%9, %7}], [%1];\n\t}"
-        ::"r"((int)leader), "r"(bar), "r"(bytes), "r"(dst), "l"(map), "r"(c0 * 64), "r"(two),
-          "r"(row0), "r"(dst + kChunkBytes), "r"(c0 * 64 + 64)
+        " [%10], [%4, {%11, %7}], [%1];\n\t"
+        "@l3 cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%12], [%4, {%13, %7}], [%1];\n\t}"
+        ::"r"((int)leader), "r"(bar), "r"((uint32_t)n * kChunkBytes), "r"(dst), "l"(map), "r"(x0),
+          "r"(n), "r"(row0), "r"(dst + kChunkBytes), "r"(x0 + 64), "r"(dst + 2 * kChunkBytes),
+          "r"(x0 + 128), "r"(dst + 3 * kChunkBytes), "r"(x0 + 192)
         : "memory");
-    ++cu.pr;
+    cu.c += n;
     cursor_settle(P, cu, warp);
 }
 
@@ -199,30 +213,47 @@ __device__ __forceinline__ void issue_scales(const Params& P, int tile, __half* 
     sm100::bulk_g2s(dst, pr.scales + (size_t)row0 * (pr.K / P.gs), bytes, bar);
 }
 
-// Staged activation layout: within each 128-k chunk the sixteen 8-element
-// blocks b = 4t + j (k = 32t + 8j) are stored at position 4j + t, each block
-// permuted to fragment order (x0x4, x1x5, x2x6, x3x7); a lane's LDS.128 for
-// word j then hits 16 consecutive bytes per t (conflict-free).
-__device__ __forceinline__ void stage_activations(const Params& P, int pi, __nv_bfloat16* xs) {
+// Staged activations (only when they fit): within each 128-k chunk the
+// sixteen 8-element blocks b = 4t + j (k = 32t + 8j) are stored at position
+// 4j + t, each block permuted to (x0x4, x1x5, x2x6, x3x7); a lane's LDS.128
+// for word j then hits 16 consecutive bytes per t (conflict-free).  The same
+// pass forms the per-chunk sums sx[c][m] = sum of the chunk's 128 bf16 x[m, k]
+// (fp32; the 16 blocks of a chunk sit in 16 consecutive threads, reduced by
+// shuffles), and zeroes the columns m >= M.
+__device__ __forceinline__ void stage_activations(const Params& P, int pi, float* sx,
+                                                  __nv_bfloat16* xs) {
     const Prob& pr = P.p[pi];
     const int nb = pr.K / 8;
     const int blocks = P.M * nb;
-    for (int b = threadIdx.x; b < blocks; b += kThreads) {
-        const int m = b / nb, kb = b - m * nb;
-        const uint4 v = kc_ldg_keep(pr.x + (size_t)m * pr.K + kb * 8);
+    const int C = pr.K >> 7;
+    for (int i = threadIdx.x; i < C * kSxCols; i += kThreads)
+        if (i % kSxCols >= P.M) sx[i] = 0.f;
+    const int rounds = (blocks + 31) & ~31;   // whole warps: the shuffles need every lane
+    for (int b = threadIdx.x; b < rounds; b += kThreads) {
+        const bool valid = b < blocks;
+        const int m = valid ? b / nb : 0, kb = valid ? b - m * nb : 0;
+        const uint4 v = valid ? kc_ldg_keep(pr.x + (size_t)m * pr.K + kb * 8) : make_uint4(0, 0, 0, 0);
+        float sum = 0.f;
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sum += __uint_as_float(w4[i] << 16) + __uint_as_float(w4[i] & 0xFFFF0000u);
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (!valid) continue;
         const uint4 o = make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
                                    prmt(v.y, v.w, 0x5410u), prmt(v.y, v.w, 0x7632u));
         const int c = kb >> 4, r = kb & 15;
         const int pos = (c << 4) + ((r & 3) << 2) + (r >> 2);
         *reinterpret_cast<uint4*>(xs + (size_t)m * P.xs_row + pos * 8) = o;
+        if (r == 0) sx[c * kSxCols + m] = sum;
     }
 }
 
-// One 128-k chunk of one lane: rows g, g+8 (words wa, wb), activations X.
+// One 128-k chunk of one lane: rows g, g+8 (words WA, WB), activations X;
+// accumulates sum (128 + u) x into cm (staged), or sum (u - 8) x (unstaged).
 template <int NT, bool XS>
 __device__ __forceinline__ void chunk_mma(const uint4& WA, const uint4& WB, const uint4 (&X)[NT][4],
-                                          uint32_t magic, uint32_t neg136, float (&cm)[NT][4],
-                                          float (&cc)[NT][4]) {
+                                          uint32_t magic, uint32_t neg136, float (&cm)[NT][4]) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t wa = j == 0 ? WA.x : j == 1 ? WA.y : j == 2 ? WA.z : WA.w;
@@ -245,7 +276,9 @@ __device__ __forceinline__ void chunk_mma(const uint4& WA, const uint4& WB, cons
                     b1 = prmt(lo, hi, 0x7632u);
                 }
                 mma_16816(cm[nt], A[2 * h], B[2 * h], A[2 * h + 1], B[2 * h + 1], b0, b1);
-                mma_16816(cc[nt], neg136, neg136, neg136, neg136, b0, b1);
+                // unstaged activations have no precomputed sums: the offset is
+                // removed by a second MMA with the constant fragment -136
+                if (!XS) mma_16816(cm[nt], neg136, neg136, neg136, neg136, b0, b1);
             }
         }
     }
@@ -270,7 +303,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w4a16_kernel(const __grid_co
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     using SM = Smem<NT>;
     SM& S = *reinterpret_cast<SM*>(smem_raw);
-    __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem_raw + fixed_smem<NT>());
+    float* sx = reinterpret_cast<float*>(smem_raw + fixed_smem<NT>());
+    __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sx + (size_t)P.sx_chunks * kSxCols);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int M = P.M, gshift = P.gshift, gs = P.gs, total = P.total_tiles;
@@ -286,21 +320,21 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w4a16_kernel(const __grid_co
     __syncthreads();
     if ((int)blockIdx.x >= total) return;
 
-    // prologue: the first tile's scales, and the first kRing pairs of every warp
+    // prologue: the first tile's scales, and the first kRing quads of every warp
     if (threadIdx.x == 0) issue_scales(P, blockIdx.x, S.scales[0], &S.sfull[0]);
     Cursor pf;
     pf.tile = blockIdx.x;
     pf.pi = problem_index(P, pf.tile);
-    pf.chunks = P.p[pf.pi].K >> 7;
-    warp_pairs(pf.chunks, warp, pf.pr, pf.pend);
+    warp_chunks(P.p[pf.pi].K >> 7, warp, pf.c, pf.cend);
     cursor_settle(P, pf, warp);
     const bool leader = lane == 0;
     const uint32_t ring0 = sm100::smem_u32(&S.ring[warp][0][0][0]);
     const uint32_t bar0 = sm100::smem_u32(&S.wfull[warp][0]);
     for (int s = 0; s < kRing; ++s)
-        issue_pair(P, pf, ring0 + s * 2 * kChunkBytes, bar0 + 8 * s, warp, leader);
+        issue_quad(P, pf, ring0 + s * kQuad * kChunkBytes, bar0 + 8 * s, warp, leader);
 
-    const uint32_t ring_base = sm100::smem_u32(&S.ring[warp][0][0][0]) + g * 64 + 16 * t;
+    const uint32_t ring_base = ring0 + g * 64 + 16 * t;
+    const uint32_t sx_base = sm100::smem_u32(sx) + 8 * t;  // columns 2t, 2t+1 (+8 nt)
     uint32_t it = 0, ti = 0;
     int staged = -1;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
@@ -309,7 +343,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w4a16_kernel(const __grid_co
         const int N = pr.N, K = pr.K, C = K >> 7;
         const int row0 = (tile - pr.tile_begin) * 16;
         if (XS && pi != staged) {
-            stage_activations(P, pi, xs);  // every warp finished the previous tile (its barrier)
+            stage_activations(P, pi, sx, xs);  // every warp passed the previous tile's barrier
             __syncthreads();
             staged = pi;
         }
@@ -339,66 +373,50 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w4a16_kernel(const __grid_co
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 
-        int p_begin, p_end;
-        warp_pairs(C, warp, p_begin, p_end);
-        for (int pp = p_begin; pp < p_end; ++pp, ++it) {
-            const uint32_t s = it & (kRing - 1), ph = (it / kRing) & 1u;
-            const int c0 = 2 * pp;
-            const uint32_t st = ring_base + s * (2 * kChunkBytes);
-            if (c0 + 1 < C) {  // full pair (always when K % 256 == 0)
-                const float sa0 = lds_half(sa_base + 2 * (c0 >> gshift));
-                const float sb0 = lds_half(sb_base + 2 * (c0 >> gshift));
-                const float sa1 = lds_half(sa_base + 2 * ((c0 + 1) >> gshift));
-                const float sb1 = lds_half(sb_base + 2 * ((c0 + 1) >> gshift));
-                uint4 X0[NT][4], X1[NT][4];
-                load_x<NT, XS>(xrow, xsb, c0, X0);
-                load_x<NT, XS>(xrow, xsb, c0 + 1, X1);
-                    sm100::mbar_wait(&S.wfull[warp][s], ph);
-                const uint4 WA0 = lds128(st), WB0 = lds128(st + 512);
-                const uint4 WA1 = lds128(st + kChunkBytes), WB1 = lds128(st + kChunkBytes + 512);
-                float cm0[NT][4], cc0[NT][4], cm1[NT][4], cc1[NT][4];
+        int c_begin, c_end;
+        warp_chunks(C, warp, c_begin, c_end);
+        for (int q0 = c_begin; q0 < c_end; q0 += kQuad, ++it) {
+            const uint32_t s = it % kRing, ph = (it / kRing) & 1u;
+            const int nq = min(kQuad, c_end - q0);
+            const uint32_t st = ring_base + s * (kQuad * kChunkBytes);
+            sm100::mbar_wait(&S.wfull[warp][s], ph);
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+            for (int j = 0; j < kQuad; ++j) {
+                if (j < nq) {
+                    const int c = q0 + j;
+                    const int grp = c >> gshift;
+                    const float sa = lds_half(sa_base + 2 * grp);
+                    const float sb2 = lds_half(sb_base + 2 * grp);
+                    uint4 X[NT][4];
+                    load_x<NT, XS>(xrow, xsb, c, X);
+                    const uint4 WA = lds128(st + j * kChunkBytes);
+                    const uint4 WB = lds128(st + j * kChunkBytes + 512);
+                    float cm[NT][4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) cm0[nt][e] = cc0[nt][e] = cm1[nt][e] = cc1[nt][e] = 0.f;
-                chunk_mma<NT, XS>(WA0, WB0, X0, magic, neg136, cm0, cc0);
-                chunk_mma<NT, XS>(WA1, WB1, X1, magic, neg136, cm1, cc1);
+                    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    acc[nt][0] = fmaf(sa0, cm0[nt][0] + cc0[nt][0], acc[nt][0]);
-                    acc[nt][1] = fmaf(sa0, cm0[nt][1] + cc0[nt][1], acc[nt][1]);
-                    acc[nt][2] = fmaf(sb0, cm0[nt][2] + cc0[nt][2], acc[nt][2]);
-                    acc[nt][3] = fmaf(sb0, cm0[nt][3] + cc0[nt][3], acc[nt][3]);
-                    acc[nt][0] = fmaf(sa1, cm1[nt][0] + cc1[nt][0], acc[nt][0]);
-                    acc[nt][1] = fmaf(sa1, cm1[nt][1] + cc1[nt][1], acc[nt][1]);
-                    acc[nt][2] = fmaf(sb1, cm1[nt][2] + cc1[nt][2], acc[nt][2]);
-                    acc[nt][3] = fmaf(sb1, cm1[nt][3] + cc1[nt][3], acc[nt][3]);
-                }
-            } else {  // the row's last, unpaired chunk
-                const float sa0 = lds_half(sa_base + 2 * (c0 >> gshift));
-                const float sb0 = lds_half(sb_base + 2 * (c0 >> gshift));
-                uint4 X0[NT][4];
-                load_x<NT, XS>(xrow, xsb, c0, X0);
-                sm100::mbar_wait(&S.wfull[warp][s], ph);
-                const uint4 WA0 = lds128(st), WB0 = lds128(st + 512);
-                float cm0[NT][4], cc0[NT][4];
+                        for (int e = 0; e < 4; ++e) cm[nt][e] = 0.f;
+                    chunk_mma<NT, XS>(WA, WB, X, magic, neg136, cm);
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) cm0[nt][e] = cc0[nt][e] = 0.f;
-                chunk_mma<NT, XS>(WA0, WB0, X0, magic, neg136, cm0, cc0);
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    acc[nt][0] = fmaf(sa0, cm0[nt][0] + cc0[nt][0], acc[nt][0]);
-                    acc[nt][1] = fmaf(sa0, cm0[nt][1] + cc0[nt][1], acc[nt][1]);
-                    acc[nt][2] = fmaf(sb0, cm0[nt][2] + cc0[nt][2], acc[nt][2]);
-                    acc[nt][3] = fmaf(sb0, cm0[nt][3] + cc0[nt][3], acc[nt][3]);
+                    for (int nt = 0; nt < NT; ++nt) {
+                        // staged: minus 136 * sum x of this chunk (columns 2t, 2t+1 of tile nt)
+                        float c0 = 0.f, c1 = 0.f;
+                        if (XS) {
+                            const float2 sxv = lds_f2(sx_base + (c * kSxCols + nt * 8) * 4);
+                            c0 = 136.f * sxv.x;
+                            c1 = 136.f * sxv.y;
+                        }
+                        acc[nt][0] = fmaf(sa, cm[nt][0] - c0, acc[nt][0]);
+                        acc[nt][1] = fmaf(sa, cm[nt][1] - c1, acc[nt][1]);
+                        acc[nt][2] = fmaf(sb2, cm[nt][2] - c0, acc[nt][2]);
+                        acc[nt][3] = fmaf(sb2, cm[nt][3] - c1, acc[nt][3]);
+                    }
                 }
             }
-            // the stage is consumed: refill it with the pair kRing ahead
+            // the stage is consumed: refill it with the quad kRing ahead
             __syncwarp();
             if (leader) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_pair(P, pf, ring0 + s * 2 * kChunkBytes, bar0 + 8 * s, warp, leader);
+            issue_quad(P, pf, ring0 + s * kQuad * kChunkBytes, bar0 + 8 * s, warp, leader);
         }
         // cross-warp reduction of the tile
 #pragma unroll
@@ -456,7 +474,7 @@ __global__ void __launch_bounds__(256) gemv_w4a16_scalar(const __grid_constant__
 
 template <int NT, bool XS>
 int launch_tc(const Params& P, size_t xs_bytes, cudaStream_t stream) {
-    const size_t smem = fixed_smem<NT>() + xs_bytes;
+    const size_t smem = fixed_smem<NT>() + (size_t)P.sx_chunks * kSxCols * 4 + xs_bytes;
     auto kern = gemv_w4a16_kernel<NT, XS>;
     KC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "gemv_w4a16 shared-memory attribute");
@@ -513,6 +531,7 @@ int launch(Params& P, cudaStream_t stream) {
     }
     const size_t xs_bytes = (size_t)P.M * kmax * 2;
     const bool stage = xs_bytes <= kMaxStagedActivationBytes;
+    P.sx_chunks = stage ? kmax / 128 : 0;
     P.xs_row = stage ? kmax : 0;
     if (P.M <= 8)
         return stage ? launch_tc<1, true>(P, xs_bytes, stream) : launch_tc<1, false>(P, 0, stream);

@@ -51,6 +51,8 @@ struct Prob {
     float* y;
     int N, K;
     int tile_begin;  // first 16-row tile of this problem in the flattened tile list
+    int xs_off;      // staged activations: byte offset of this problem's rows in shared memory
+    int sx_off;      // staged chunk sums: first chunk row of this problem
 };
 
 struct alignas(64) Params {
@@ -61,29 +63,37 @@ struct alignas(64) Params {
     int M;
     int gs;
     int gshift;      // group of 128-k chunk c is c >> gshift
-    int xs_row;      // row pitch (elements) of the staged activations, 0 = not staged
-    int sx_chunks;   // chunk capacity of the staged activation sums
+    int stage_bytes;   // staged activation bytes copied (all problems), 0 = not staged
+    int sx_chunks;     // chunk rows of the staged activation sums (all problems)
     uint32_t magic;  // 0x43004300 = bf16x2 (128, 128), held in a register (see nib_or)
     uint32_t neg136; // 0xC308C308 = bf16x2 (-136, -136): the unstaged path's offset MMA fragment
 };
 
-constexpr int kWarps = 8;
+constexpr int kGroupWarps = 8;                    // warps that split one tile's K range
+constexpr int kGroups = 2;                        // independent tile groups per CTA
+constexpr int kWarps = kGroupWarps * kGroups;
 constexpr int kThreads = kWarps * 32;
+constexpr int kGroupThreads = kGroupWarps * 32;
 constexpr int kChunkBytes = 1024;                 // 16 rows x 64 bytes = 128 k
 constexpr int kQuad = 4;                          // chunks per stage
 constexpr int kRing = 2;                          // stages per warp
 constexpr int kScaleHalves = 16 * 128;            // 16 rows x up to 128 groups
-constexpr int kSxCols = 16;                       // activation-sum columns (M padded)
+constexpr int kScaleBufs = 3;                     // scale blocks in flight per group
 
 template <int NT>
 struct Smem {
     uint8_t ring[kWarps][kRing][kQuad][kChunkBytes];  // TMA destinations, 1024-byte aligned
-    __half scales[2][kScaleHalves];
-    float red[kWarps][16][NT * 8 + 1];
+    __half scales[kGroups][kScaleBufs][kScaleHalves];
+    float red[kGroups][2][kGroupWarps][16][NT * 8 + 1];  // double-buffered by tile parity
     uint64_t wfull[kWarps][kRing];
-    uint64_t sfull[2];
-    // then, if staged: the activation sums float[sx_chunks][kSxCols] and the
-    // activations (bf16, fragment order), 16-byte aligned
+    uint64_t sfull[kGroups][kScaleBufs];
+    uint64_t xfull;            // staged activations landed
+    int red_cnt[kGroups][2];   // warps that stored their partials for the slot's tile
+    int red_done[kGroups][2];  // group tile counter of the last tile reduced from the slot
+    // then, if staged: the chunk sums float[sx_chunks][NT * 8], and the
+    // activations of every problem, row m of problem i at
+    // xs_off(i) + m * (2K + 16) bytes (the pad spreads rows over the banks),
+    // permuted in place to fragment order after they land
 };
 
 template <int NT>
@@ -151,10 +161,10 @@ __device__ __forceinline__ int problem_index(const Params& P, int tile) {
     return pi;
 }
 
-// Chunk range [begin, end) of warp w for a row of C 128-k chunks.
+// Chunk range [begin, end) of group warp w for a row of C 128-k chunks.
 __device__ __forceinline__ void warp_chunks(int C, int w, int& begin, int& end) {
-    begin = (w * C) >> 3;
-    end = ((w + 1) * C) >> 3;
+    begin = (w * C) / kGroupWarps;
+    end = ((w + 1) * C) / kGroupWarps;
 }
 
 // A warp's position in its own sequence of (tile, quad) work items.
@@ -162,9 +172,11 @@ struct Cursor {
     int tile, c, cend, pi;
 };
 
+// Tiles of a group: vg, vg + G, vg + 2G, ... with vg = 2 * blockIdx + group
+// and G = 2 * gridDim (every (CTA, group) pair walks its own tile sequence).
 __device__ __forceinline__ void cursor_settle(const Params& P, Cursor& cu, int warp) {
     while (cu.tile < P.total_tiles && cu.c >= cu.cend) {
-        cu.tile += gridDim.x;
+        cu.tile += kGroups * gridDim.x;
         if (cu.tile >= P.total_tiles) break;
         cu.pi = problem_index(P, cu.tile);
         warp_chunks(P.p[cu.pi].K >> 7, warp, cu.c, cu.cend);
@@ -213,47 +225,22 @@ __device__ __forceinline__ void issue_scales(const Params& P, int tile, __half* 
     sm100::bulk_g2s(dst, pr.scales + (size_t)row0 * (pr.K / P.gs), bytes, bar);
 }
 
-// Staged activations (only when they fit): within each 128-k chunk the
-// sixteen 8-element blocks b = 4t + j (k = 32t + 8j) are stored at position
-// 4j + t, each block permuted to (x0x4, x1x5, x2x6, x3x7); a lane's LDS.128
-// for word j then hits 16 consecutive bytes per t (conflict-free).  The same
-// pass forms the per-chunk sums sx[c][m] = sum of the chunk's 128 bf16 x[m, k]
-// (fp32; the 16 blocks of a chunk sit in 16 consecutive threads, reduced by
-// shuffles), and zeroes the columns m >= M.
-__device__ __forceinline__ void stage_activations(const Params& P, int pi, float* sx,
-                                                  __nv_bfloat16* xs) {
-    const Prob& pr = P.p[pi];
-    const int nb = pr.K / 8;
-    const int blocks = P.M * nb;
-    const int C = pr.K >> 7;
-    for (int i = threadIdx.x; i < C * kSxCols; i += kThreads)
-        if (i % kSxCols >= P.M) sx[i] = 0.f;
-    const int rounds = (blocks + 31) & ~31;   // whole warps: the shuffles need every lane
-    for (int b = threadIdx.x; b < rounds; b += kThreads) {
-        const bool valid = b < blocks;
-        const int m = valid ? b / nb : 0, kb = valid ? b - m * nb : 0;
-        const uint4 v = valid ? kc_ldg_keep(pr.x + (size_t)m * pr.K + kb * 8) : make_uint4(0, 0, 0, 0);
-        float sum = 0.f;
-        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sum += __uint_as_float(w4[i] << 16) + __uint_as_float(w4[i] & 0xFFFF0000u);
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (!valid) continue;
-        const uint4 o = make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
-                                   prmt(v.y, v.w, 0x5410u), prmt(v.y, v.w, 0x7632u));
-        const int c = kb >> 4, r = kb & 15;
-        const int pos = (c << 4) + ((r & 3) << 2) + (r >> 2);
-        *reinterpret_cast<uint4*>(xs + (size_t)m * P.xs_row + pos * 8) = o;
-        if (r == 0) sx[c * kSxCols + m] = sum;
-    }
-}
-
-// One 128-k chunk of one lane: rows g, g+8 (words WA, WB), activations X;
-// accumulates sum (128 + u) x into cm (staged), or sum (u - 8) x (unstaged).
+// One 128-k chunk of one lane: rows g, g+8 (words WA, WB), activations X.
+// Staged (XS): X is in fragment order (x0x4, x1x5, x2x6, x3x7 per 8-block) and
+// cm receives sum (128 + u) x; the offset is removed by the caller with the
+// chunk's activation sum.  Unstaged: X is in natural order (x0x1, x2x3, x4x5,
+// x6x7), paired with PRMT, and a second MMA with the constant fragment -136
+// removes the offset, so cm receives sum (u - 8) x.  The MMAs of a chunk feed
+// independent accumulators (per k half of each word, weights and offset
+// apart), so no MMA waits on the one before it.
 template <int NT, bool XS>
 __device__ __forceinline__ void chunk_mma(const uint4& WA, const uint4& WB, const uint4 (&X)[NT][4],
                                           uint32_t magic, uint32_t neg136, float (&cm)[NT][4]) {
+    float c1[NT][4], o0[NT][4], o1[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) c1[nt][e] = o0[nt][e] = o1[nt][e] = 0.f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t wa = j == 0 ? WA.x : j == 1 ? WA.y : j == 2 ? WA.z : WA.w;
@@ -266,26 +253,71 @@ __device__ __forceinline__ void chunk_mma(const uint4& WA, const uint4& WB, cons
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 uint32_t b0, b1;
-                if (XS) {  // staged in fragment order
+                if (XS) {
                     b0 = h ? X[nt][j].z : X[nt][j].x;
                     b1 = h ? X[nt][j].w : X[nt][j].y;
-                } else {   // natural order: (x0x1, x2x3, x4x5, x6x7)
+                } else {
                     const uint32_t lo = h ? X[nt][j].y : X[nt][j].x;
                     const uint32_t hi = h ? X[nt][j].w : X[nt][j].z;
                     b0 = prmt(lo, hi, 0x5410u);
                     b1 = prmt(lo, hi, 0x7632u);
                 }
-                mma_16816(cm[nt], A[2 * h], B[2 * h], A[2 * h + 1], B[2 * h + 1], b0, b1);
-                // unstaged activations have no precomputed sums: the offset is
-                // removed by a second MMA with the constant fragment -136
-                if (!XS) mma_16816(cm[nt], neg136, neg136, neg136, neg136, b0, b1);
+                mma_16816(h ? c1[nt] : cm[nt], A[2 * h], B[2 * h], A[2 * h + 1], B[2 * h + 1], b0, b1);
+                if (!XS) mma_16816(h ? o1[nt] : o0[nt], neg136, neg136, neg136, neg136, b0, b1);
+            }
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            cm[nt][e] += XS ? c1[nt][e] : (c1[nt][e] + (o0[nt][e] + o1[nt][e]));
+}
+
+// In-place pass over the staged activations (natural order on arrival): each
+// 8-element block is permuted to fragment order, and within each 128-k chunk
+// the sixteen blocks b = 4t + j (k = 32t + 8j) move to position 4j + t, so a
+// lane's LDS.128 for word j hits 16 consecutive bytes per t.  The same pass
+// forms the per-chunk sums sx[c][m] (fp32).  A chunk's 16 blocks belong to 16
+// consecutive threads of one warp, which read before any of them writes.
+template <int NT>
+__device__ __forceinline__ void permute_staged(const Params& P, uint8_t* xs, float* sx) {
+    constexpr int kCols = NT * 8;
+    for (int i = threadIdx.x; i < P.sx_chunks * kCols; i += kThreads) sx[i] = 0.f;
+    __syncthreads();
+    for (int pi = 0; pi < P.count; ++pi) {
+        const Prob& pr = P.p[pi];
+        const int nb = pr.K >> 3;                    // a multiple of 16
+        const int rounds = (nb + 31) & ~31;          // whole warps: the shuffles need every lane
+        for (int m = 0; m < P.M; ++m) {
+            uint8_t* row = xs + pr.xs_off + (size_t)m * (2 * pr.K + 16);
+            for (int kb = threadIdx.x; kb < rounds; kb += kThreads) {
+                const bool valid = kb < nb;
+                const uint4 v = valid ? *reinterpret_cast<const uint4*>(row + kb * 16) : make_uint4(0, 0, 0, 0);
+                float sum = 0.f;
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    sum += __uint_as_float(w4[i] << 16) + __uint_as_float(w4[i] & 0xFFFF0000u);
+#pragma unroll
+                for (int o = 8; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                __syncwarp();   // the chunk's blocks are all read before any is rewritten
+                if (valid) {
+                    const int c = kb >> 4, r = kb & 15;
+                    const int pos = (c << 4) + ((r & 3) << 2) + (r >> 2);
+                    *reinterpret_cast<uint4*>(row + pos * 16) =
+                        make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
+                                   prmt(v.y, v.w, 0x5410u), prmt(v.y, v.w, 0x7632u));
+                    if (r == 0) sx[(pr.sx_off + c) * kCols + m] = sum;
+                }
             }
         }
     }
 }
 
-// B fragments of chunk c: staged (xsb = shared address of this lane's clamped
-// activation row + 16 t) or from global memory (xrow = clamped row + 32 t).
+// Activations of chunk c for this lane's B fragments: from shared memory in
+// fragment order (xsb = this lane's clamped row + 16 t; block 4j + t) or from
+// global memory in natural order (xrow = clamped row + 32 t; k = 32 t + 8 j).
 template <int NT, bool XS>
 __device__ __forceinline__ void load_x(const __nv_bfloat16* const (&xrow)[NT],
                                        const uint32_t (&xsb)[NT], int c, uint4 (&X)[NT][4]) {
@@ -299,63 +331,88 @@ __device__ __forceinline__ void load_x(const __nv_bfloat16* const (&xrow)[NT],
 }
 
 template <int NT, bool XS>
-__global__ void __launch_bounds__(kThreads, 2) gemv_w4a16_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(kThreads, 1) gemv_w4a16_kernel(const __grid_constant__ Params P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     using SM = Smem<NT>;
+    constexpr int kCols = NT * 8;
     SM& S = *reinterpret_cast<SM*>(smem_raw);
     float* sx = reinterpret_cast<float*>(smem_raw + fixed_smem<NT>());
-    __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sx + (size_t)P.sx_chunks * kSxCols);
+    uint8_t* xs = reinterpret_cast<uint8_t*>(sx + (size_t)P.sx_chunks * kCols);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int group = warp / kGroupWarps, gw = warp % kGroupWarps;
+    const int gtid = threadIdx.x % kGroupThreads;
     const int g = lane >> 2, t = lane & 3;
     const int M = P.M, gshift = P.gshift, gs = P.gs, total = P.total_tiles;
     const uint32_t magic = P.magic, neg136 = P.neg136;
+    const int first = kGroups * blockIdx.x + group, stride = kGroups * gridDim.x;
 
+    // the next launch in the stream may start its prologue while this grid drains
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (threadIdx.x == 0) {
         for (int w = 0; w < kWarps; ++w)
             for (int i = 0; i < kRing; ++i) sm100::mbar_init(&S.wfull[w][i], 1);
-        sm100::mbar_init(&S.sfull[0], 1);
-        sm100::mbar_init(&S.sfull[1], 1);
+        for (int h = 0; h < kGroups; ++h) {
+            for (int i = 0; i < kScaleBufs; ++i) sm100::mbar_init(&S.sfull[h][i], 1);
+            S.red_cnt[h][0] = S.red_cnt[h][1] = 0;
+            S.red_done[h][0] = S.red_done[h][1] = -1;
+        }
+        sm100::mbar_init(&S.xfull, 1);
         sm100::fence_barrier_init();
     }
     __syncthreads();
-    if ((int)blockIdx.x >= total) return;
 
-    // prologue: the first tile's scales, and the first kRing quads of every warp
-    if (threadIdx.x == 0) issue_scales(P, blockIdx.x, S.scales[0], &S.sfull[0]);
+    // prologue: the group's first kScaleBufs scale blocks and the first kRing
+    // weight quads of every warp.  Weights and scales are issued before the
+    // wait on the previous grid: they are layer constants that no kernel of
+    // this library writes, so the loads overlap the previous grid's drain.
+    if (gtid == 0)
+        for (int i = 0; i < kScaleBufs && first + i * stride < total; ++i)
+            issue_scales(P, first + i * stride, S.scales[group][i], &S.sfull[group][i]);
     Cursor pf;
-    pf.tile = blockIdx.x;
-    pf.pi = problem_index(P, pf.tile);
-    warp_chunks(P.p[pf.pi].K >> 7, warp, pf.c, pf.cend);
-    cursor_settle(P, pf, warp);
+    pf.tile = first;
+    pf.c = pf.cend = 0;
+    pf.pi = 0;
+    if (pf.tile < total) {
+        pf.pi = problem_index(P, pf.tile);
+        warp_chunks(P.p[pf.pi].K >> 7, gw, pf.c, pf.cend);
+        cursor_settle(P, pf, gw);
+    }
     const bool leader = lane == 0;
     const uint32_t ring0 = sm100::smem_u32(&S.ring[warp][0][0][0]);
     const uint32_t bar0 = sm100::smem_u32(&S.wfull[warp][0]);
     for (int s = 0; s < kRing; ++s)
-        issue_quad(P, pf, ring0 + s * kQuad * kChunkBytes, bar0 + 8 * s, warp, leader);
+        issue_quad(P, pf, ring0 + s * kQuad * kChunkBytes, bar0 + 8 * s, gw, leader);
+
+    // the activations (and y) may be produced / consumed by the previous grid
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (XS) {
+        // one bulk copy per activation row, all landing on one barrier
+        if (threadIdx.x == 0) {
+            sm100::mbar_arrive_expect_tx(&S.xfull, (uint32_t)P.stage_bytes);
+            for (int i = 0; i < P.count; ++i) {
+                const Prob& q = P.p[i];
+                for (int m = 0; m < M; ++m)
+                    sm100::bulk_g2s(xs + q.xs_off + (size_t)m * (2 * q.K + 16), q.x + (size_t)m * q.K,
+                                    (uint32_t)(2 * q.K), &S.xfull);
+            }
+        }
+        sm100::mbar_wait(&S.xfull, 0);
+        permute_staged<NT>(P, xs, sx);
+        __syncthreads();
+    }
+    const uint32_t sx_base = sm100::smem_u32(sx) + 8 * t;  // columns 2t, 2t+1 (+8 nt)
 
     const uint32_t ring_base = ring0 + g * 64 + 16 * t;
-    const uint32_t sx_base = sm100::smem_u32(sx) + 8 * t;  // columns 2t, 2t+1 (+8 nt)
     uint32_t it = 0, ti = 0;
-    int staged = -1;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++ti) {
+    for (int tile = first; tile < total; tile += stride, ++ti) {
         const int pi = problem_index(P, tile);
         const Prob& pr = P.p[pi];
         const int N = pr.N, K = pr.K, C = K >> 7;
         const int row0 = (tile - pr.tile_begin) * 16;
-        if (XS && pi != staged) {
-            stage_activations(P, pi, sx, xs);  // every warp passed the previous tile's barrier
-            __syncthreads();
-            staged = pi;
-        }
-        const uint32_t sb = ti & 1u;
-        sm100::mbar_wait(&S.sfull[sb], (ti >> 1) & 1u);
-        if (threadIdx.x == 0 && tile + (int)gridDim.x < total) {
-            // the other buffer's generic reads (previous tile) precede this async write
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_scales(P, tile + gridDim.x, S.scales[sb ^ 1u], &S.sfull[sb ^ 1u]);
-        }
+        const uint32_t sb = ti % kScaleBufs;
+        sm100::mbar_wait(&S.sfull[group][sb], (ti / kScaleBufs) & 1u);
         const int G = K / gs;
-        const uint32_t sa_base = sm100::smem_u32(&S.scales[sb][g * G]);
+        const uint32_t sa_base = sm100::smem_u32(&S.scales[group][sb][g * G]);
         const uint32_t sb_base = sa_base + 16 * G;  // row g + 8
         // activation rows of this lane's B fragments (columns >= M read row M - 1, discarded)
         const __nv_bfloat16* xrow[NT];
@@ -364,8 +421,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w4a16_kernel(const __grid_co
         for (int nt = 0; nt < NT; ++nt) {
             const int n = min(nt * 8 + g, M - 1);
             xrow[nt] = pr.x + (size_t)n * K + 32 * t;
-            xsb[nt] = XS ? sm100::smem_u32(xs + (size_t)n * P.xs_row) + 16 * t : 0u;
+            xsb[nt] = XS ? sm100::smem_u32(xs + pr.xs_off + (size_t)n * (2 * K + 16)) + 16 * t : 0u;
         }
+        const uint32_t sxp = sx_base + (uint32_t)pr.sx_off * kCols * 4;
 
         float acc[NT][4];
 #pragma unroll
@@ -374,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w4a16_kernel(const __grid_co
             for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 
         int c_begin, c_end;
-        warp_chunks(C, warp, c_begin, c_end);
+        warp_chunks(C, gw, c_begin, c_end);
         for (int q0 = c_begin; q0 < c_end; q0 += kQuad, ++it) {
             const uint32_t s = it % kRing, ph = (it / kRing) & 1u;
             const int nq = min(kQuad, c_end - q0);
@@ -402,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w4a16_kernel(const __grid_co
                         // staged: minus 136 * sum x of this chunk (columns 2t, 2t+1 of tile nt)
                         float c0 = 0.f, c1 = 0.f;
                         if (XS) {
-                            const float2 sxv = lds_f2(sx_base + (c * kSxCols + nt * 8) * 4);
+                            const float2 sxv = lds_f2(sxp + (c * kCols + nt * 8) * 4);
                             c0 = 136.f * sxv.x;
                             c1 = 136.f * sxv.y;
                         }
@@ -416,25 +474,58 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_w4a16_kernel(const __grid_co
             // the stage is consumed: refill it with the quad kRing ahead
             __syncwarp();
             if (leader) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_quad(P, pf, ring0 + s * kQuad * kChunkBytes, bar0 + 8 * s, warp, leader);
+            issue_quad(P, pf, ring0 + s * kQuad * kChunkBytes, bar0 + 8 * s, gw, leader);
         }
-        // cross-warp reduction of the tile
+        // Cross-warp reduction without a barrier: each warp stores its partials
+        // in the slot of this tile's parity and counts itself in; the warp that
+        // arrives last sums the slot, writes y, refills this tile's scale
+        // buffer (every warp of the group is past its reads) and releases the
+        // slot for the tile two ahead.
+        const uint32_t slot = ti & 1u;
+        if (ti >= 2 && lane == 0) {
+            volatile int* done = &S.red_done[group][slot];
+            const uint64_t t0 = sm100::globaltimer();
+            while (*done != (int)ti - 2) {
+                if (sm100::globaltimer() - t0 > KC_WAIT_TIMEOUT_NS) {
+                    sm100::record_status(KC_ERR_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __syncwarp();
+        auto& red = S.red[group][slot];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            S.red[warp][g][nt * 8 + 2 * t]         = acc[nt][0];
-            S.red[warp][g][nt * 8 + 2 * t + 1]     = acc[nt][1];
-            S.red[warp][g + 8][nt * 8 + 2 * t]     = acc[nt][2];
-            S.red[warp][g + 8][nt * 8 + 2 * t + 1] = acc[nt][3];
+            red[gw][g][nt * 8 + 2 * t]         = acc[nt][0];
+            red[gw][g][nt * 8 + 2 * t + 1]     = acc[nt][1];
+            red[gw][g + 8][nt * 8 + 2 * t]     = acc[nt][2];
+            red[gw][g + 8][nt * 8 + 2 * t + 1] = acc[nt][3];
         }
-        __syncthreads();
-        for (int i = threadIdx.x; i < 16 * M; i += kThreads) {
-            const int r = i & 15, n = i >> 4;
-            float v = 0.f;
+        __threadfence_block();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&S.red_cnt[group][slot], 1) == kGroupWarps - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence_block();
+            if (lane == 0 && tile + kScaleBufs * stride < total) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_scales(P, tile + kScaleBufs * stride, S.scales[group][sb], &S.sfull[group][sb]);
+            }
+            for (int i = lane; i < 16 * M; i += 32) {
+                const int r = i & 15, n = i >> 4;
+                float v = 0.f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w) v += S.red[w][r][n];
-            if (row0 + r < N) pr.y[(size_t)n * N + row0 + r] = v;
+                for (int w = 0; w < kGroupWarps; ++w) v += red[w][r][n];
+                if (row0 + r < N) pr.y[(size_t)n * N + row0 + r] = v;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                S.red_cnt[group][slot] = 0;
+                __threadfence_block();
+                *reinterpret_cast<volatile int*>(&S.red_done[group][slot]) = (int)ti;
+            }
         }
-        __syncthreads();
     }
 }
 
@@ -473,27 +564,36 @@ __global__ void __launch_bounds__(256) gemv_w4a16_scalar(const __grid_constant__
 
 
 template <int NT, bool XS>
-int launch_tc(const Params& P, size_t xs_bytes, cudaStream_t stream) {
-    const size_t smem = fixed_smem<NT>() + (size_t)P.sx_chunks * kSxCols * 4 + xs_bytes;
+int launch_tc(const Params& P, size_t stage_bytes, cudaStream_t stream) {
+    const size_t smem = fixed_smem<NT>() + stage_bytes;
     auto kern = gemv_w4a16_kernel<NT, XS>;
     KC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "gemv_w4a16 shared-memory attribute");
-    int per_sm = 0;
-    KC_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem),
-                "gemv_w4a16 occupancy");
-    const int grid = std::min(P.total_tiles, kc::sm_count() * std::max(per_sm, 1));
-    kern<<<grid, kThreads, smem, stream>>>(P);
-    return kc::check_launch("gemv_w4a16");
+    const int groups = (P.total_tiles + kGroups - 1) / kGroups;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)std::min(groups, kc::sm_count()));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    // programmatic dependent launch: this grid may be scheduled while the
+    // previous one drains; the kernel waits (griddepcontrol.wait) before it
+    // reads the activations or writes y (packed weights and scales are read
+    // before the wait: they must not be written by the grid just before)
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    KC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, P), "gemv_w4a16 launch");
+    return KC_OK;
 }
 
-// Largest activation block (bytes) staged in shared memory; above it the
-// activations are read from global memory.
-constexpr size_t kMaxStagedActivationBytes = 32 * 1024;
+// Shared memory left for the staged activations and their chunk sums.
+constexpr size_t kSmemLimit = 227 * 1024;
 
 int launch(Params& P, cudaStream_t stream) {
     if (P.total_tiles == 0) return KC_OK;
     bool fast = true, single_group = true;
-    int kmax = 0;
     for (int i = 0; i < P.count && fast; ++i) {
         const Prob& p = P.p[i];
         // TMA: 16-byte aligned base and row pitch; scale blocks: a tile's 16 rows
@@ -505,7 +605,6 @@ int launch(Params& P, cudaStream_t stream) {
                kc::aligned(p.scales, 16) && 16 * row_bytes <= 2L * kScaleHalves &&
                (16 * row_bytes) % 16 == 0 && (tail == 0 || (tail * row_bytes) % 16 == 0);
         single_group = single_group && (p.K == P.gs);
-        kmax = std::max(kmax, p.K);
     }
     int gshift = -1;
     for (int m = 0; m < 20; ++m)
@@ -529,13 +628,26 @@ int launch(Params& P, cudaStream_t stream) {
                                      CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st != KC_OK) return st;
     }
-    const size_t xs_bytes = (size_t)P.M * kmax * 2;
-    const bool stage = xs_bytes <= kMaxStagedActivationBytes;
-    P.sx_chunks = stage ? kmax / 128 : 0;
-    P.xs_row = stage ? kmax : 0;
-    if (P.M <= 8)
-        return stage ? launch_tc<1, true>(P, xs_bytes, stream) : launch_tc<1, false>(P, 0, stream);
-    return stage ? launch_tc<2, true>(P, xs_bytes, stream) : launch_tc<2, false>(P, 0, stream);
+    // stage every problem's activations when they all fit
+    const int NT = P.M <= 8 ? 1 : 2;
+    long xs_bytes = 0, copied = 0, chunks = 0;  // padded footprint, bytes copied
+    for (int i = 0; i < P.count; ++i) {
+        Prob& q = P.p[i];
+        q.xs_off = (int)xs_bytes;
+        q.sx_off = (int)chunks;
+        xs_bytes += (long)P.M * (2L * q.K + 16);
+        copied += (long)P.M * 2L * q.K;
+        chunks += q.K / 128;
+    }
+    const size_t fixed = NT == 1 ? fixed_smem<1>() : fixed_smem<2>();
+    const size_t sx_bytes = (size_t)chunks * NT * 8 * 4;
+    const bool stage = fixed + sx_bytes + (size_t)xs_bytes <= kSmemLimit;
+    P.stage_bytes = stage ? (int)copied : 0;
+    P.sx_chunks = stage ? (int)chunks : 0;
+    const size_t stage_bytes = stage ? sx_bytes + (size_t)xs_bytes : 0;
+    if (NT == 1)
+        return stage ? launch_tc<1, true>(P, stage_bytes, stream) : launch_tc<1, false>(P, 0, stream);
+    return stage ? launch_tc<2, true>(P, stage_bytes, stream) : launch_tc<2, false>(P, 0, stream);
 }
 
 }  // namespace
@@ -555,13 +667,19 @@ int kc_gemv_w4a16_grouped(const kc_w4a16_problem* problems, int count, int M, in
     P.count = count;
     P.M = M;
     P.gs = gs;
+    // longest rows first: the tiles of the largest K are handed out in the
+    // first rounds, so the last round of the persistent grid is short
+    int order[KC_W4A16_MAX_PROBLEMS];
+    for (int i = 0; i < count; ++i) order[i] = i;
+    std::stable_sort(order, order + count,
+                     [&](int a, int b) { return problems[a].K > problems[b].K; });
     long tiles = 0;
     for (int i = 0; i < count; ++i) {
-        const kc_w4a16_problem& q = problems[i];
+        const kc_w4a16_problem& q = problems[order[i]];
         KC_REQUIRE(q.packed && q.scales_f16 && q.x_bf16 && q.y, KC_ERR_INVALID_ARG,
-                   "problem %d has a null pointer", i);
+                   "problem %d has a null pointer", order[i]);
         KC_REQUIRE(q.N >= 0 && q.K > 0 && q.K % 2 == 0 && q.K % gs == 0, KC_ERR_INVALID_ARG,
-                   "problem %d: bad shape N=%d K=%d for group_size=%d", i, q.N, q.K, gs);
+                   "problem %d: bad shape N=%d K=%d for group_size=%d", order[i], q.N, q.K, gs);
         P.p[i].packed = q.packed;
         P.p[i].scales = reinterpret_cast<const __half*>(q.scales_f16);
         P.p[i].x = reinterpret_cast<const __nv_bfloat16*>(q.x_bf16);

@@ -19,6 +19,15 @@ pytestmark = pytest.mark.gpu
 GEMV_TOL = 1e-3
 
 
+@pytest.fixture(autouse=True)
+def _no_device_timeouts(cuda):
+    """Every kernel of a test finishes without a device-side wait giving up
+    (a bounded wait that times out still returns, so results alone would not
+    show it)."""
+    yield
+    assert kc_lib.lib().kc_get_device_status() == kc_lib.KC_OK
+
+
 def _ref_int4_case(rows, cols, gs, zeros_mode, seed):
     rng = np.random.default_rng(seed)
     packed = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
@@ -187,8 +196,11 @@ def test_w4a16_grouped_matches_single(cuda):
         probs.append((dp, ds, dx))
         singles.append(host(ops.w4a16_gemv(dp, ds, dx, gs)))
     outs = ops.w4a16_gemv_grouped(probs, gs)
+    # a grouped launch stages activations only when every problem's block fits
+    # in shared memory, so it may take the other offset path than a single
+    # launch: equal to fp32 summation-order noise, not bit for bit
     for y, s in zip(outs, singles):
-        np.testing.assert_array_equal(host(y), s)
+        assert normwise_err(host(y), s) <= 1e-5
 
 
 def test_w4a16_unaligned_takes_scalar_path(cuda):

@@ -167,13 +167,19 @@ class Workload:
     kernel = ""            # dominant kernel (ncu name)
     profile = ""           # profiles/<profile>.md / .traffic.json
 
-    def __init__(self, torch, l, dev, s_ptr, rank):
+    scaling = "weak"       # "strong" when the ranks split one problem
+
+    def __init__(self, torch, l, dev, s_ptr, rank, world=1):
         self.torch, self.l, self.dev, self.s_ptr, self.rank = torch, l, dev, s_ptr, rank
+        self.world = world
         self.gen = torch.Generator(device=dev)
         self.gen.manual_seed(1234 + rank)
 
-    def work_per_step(self) -> float:      # bytes or flops
+    def work_per_step(self) -> float:      # bytes or flops of THIS rank per step
         raise NotImplementedError
+
+    def parallelism(self) -> str:
+        return f"replicas x{self.world}"
 
     def scale(self) -> float:              # work units -> metric units
         return 1e-9 if self.unit == "GB/s" else 1e-12
@@ -206,8 +212,8 @@ class GemvW4A16(Workload):
     kernel = "gemv_w4a16"
     profile = "gemv_w4a16_7b_decode_m1"
 
-    def __init__(self, torch, l, dev, s_ptr, rank, layers=LAYERS):
-        super().__init__(torch, l, dev, s_ptr, rank)
+    def __init__(self, torch, l, dev, s_ptr, rank, world=1, layers=LAYERS):
+        super().__init__(torch, l, dev, s_ptr, rank, world)
         import kc_lib
         self.kc_lib = kc_lib
         self.n_layers = layers
@@ -304,21 +310,34 @@ class GemmW4A16(Workload):
     M, N, K = 2048, 28672, 8192
     COPIES = 2
 
-    def __init__(self, torch, l, dev, s_ptr, rank):
-        super().__init__(torch, l, dev, s_ptr, rank)
+    def __init__(self, torch, l, dev, s_ptr, rank, world=1):
+        super().__init__(torch, l, dev, s_ptr, rank, world)
         import kc_lib
         self.kc_lib = kc_lib
         M, N, K = self.M, self.N, self.K
+        self.n_shard = N // world           # column parallel: this rank's weight rows
+        xg = torch.Generator(device=dev)
+        xg.manual_seed(77)                  # activations are replicated: same on every rank
         self.sets = []
         for _ in range(self.COPIES):
-            x = torch.randn(M, K, device=dev, generator=self.gen).bfloat16()
-            p = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=self.gen)
-            s = (torch.rand(N, K // GROUP, device=dev, generator=self.gen) * 0.018 + 0.002).half()
-            out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            x = torch.randn(M, K, device=dev, generator=xg).bfloat16()
+            p = torch.randint(0, 256, (self.n_shard, K // 2), dtype=torch.uint8, device=dev,
+                              generator=self.gen)
+            s = (torch.rand(self.n_shard, K // GROUP, device=dev, generator=self.gen) * 0.018
+                 + 0.002).half()
+            out = torch.empty(M, N, dtype=torch.bfloat16, device=dev) if world == 1 else None
             self.sets.append((x, p, s, out))
+        self.col = None
+        if world > 1:
+            import tp
+            self.col = tp.ColParallelW4A16(M, N, K, GROUP)
+            self.scaling = "strong"
         self.i = 0
 
     def _launch(self, x, p, s, out):
+        if self.col is not None:   # fused GEMM + all-gather, stream barriers around it
+            self.col(x, p, s)
+            return
         self.kc_lib.check(self.l.kc_gemm_w4a16(x.data_ptr(), p.data_ptr(), s.data_ptr(),
                                                out.data_ptr(), 0, self.M, self.N, self.K, GROUP,
                                                self.N, self.s_ptr))
@@ -328,24 +347,36 @@ class GemmW4A16(Workload):
         self.i += 1
 
     def work_per_step(self):
-        return 2.0 * self.M * self.N * self.K
+        return 2.0 * self.M * self.n_shard * self.K
+
+    def parallelism(self):
+        if self.world == 1:
+            return "single GPU"
+        return (f"column parallel x{self.world}: N/{self.world} weight rows per GPU, "
+                "output tiles stored into every GPU's [M, N] buffer by the GEMM epilogue "
+                "over NVLink (fused all-gather), stream barrier (NCCL) before and after")
 
     def config(self):
         return {"workload": "w4a16-gemm-2048x28672x8192", "M": self.M, "N": self.N, "K": self.K,
                 "group_size": GROUP, "out": "bf16",
-                "l2": f"{self.COPIES} rotating operand sets of 270 MB (larger than L2)"}
+                "l2": f"{self.COPIES} rotating operand sets, each step also writes the full "
+                      "117 MB output (larger than L2)"}
+
+    def _out(self, out):
+        return self.col.out if self.col is not None else out
 
     def e2e_prepare(self):
         x, _, _, out = self.sets[0]
+        o = self._out(out)
         self.h_x = x.cpu().pin_memory()
-        self.h_out = self.torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        self.h_out = self.torch.empty(o.shape, dtype=o.dtype).pin_memory()
         return self.h_x.numel() * 2, self.h_out.numel() * 2
 
     def e2e_step(self):
         x, p, s, out = self.sets[0]
         x.copy_(self.h_x, non_blocking=True)
         self._launch(x, p, s, out)
-        self.h_out.copy_(out, non_blocking=True)
+        self.h_out.copy_(self._out(out), non_blocking=True)
 
     @classmethod
     def _cpu(cls, rows):
@@ -382,17 +413,18 @@ class GemmFP8(Workload):
     M, N, K = 4096, 8192, 8192
     COPIES = 2
 
-    def __init__(self, torch, l, dev, s_ptr, rank):
-        super().__init__(torch, l, dev, s_ptr, rank)
+    def __init__(self, torch, l, dev, s_ptr, rank, world=1):
+        super().__init__(torch, l, dev, s_ptr, rank, world)
         import kc_lib
         self.kc_lib = kc_lib
         M, N, K = self.M, self.N, self.K
+        self.k0, self.k1 = rank * K // world, (rank + 1) * K // world  # row parallel: K shard
         self.x32 = self._outlier_x(M, K)
+        self.qa_full = torch.empty(M, K, dtype=torch.int8, device=dev)
         self.sets = []
         for _ in range(self.COPIES):
-            qa = torch.empty(M, K, dtype=torch.int8, device=dev)
             sa = torch.empty(M, dtype=torch.float32, device=dev)
-            kc_lib.check(l.kc_quantize_fp8_per_token(self.x32.data_ptr(), qa.data_ptr(),
+            kc_lib.check(l.kc_quantize_fp8_per_token(self.x32.data_ptr(), self.qa_full.data_ptr(),
                                                      sa.data_ptr(), M, K, s_ptr))
             w = torch.randn(N, K, device=dev, generator=self.gen) * 0.02
             qw = torch.empty(N, K, dtype=torch.int8, device=dev)
@@ -400,8 +432,12 @@ class GemmFP8(Workload):
             kc_lib.check(l.kc_quantize_fp8_per_channel(w.data_ptr(), qw.data_ptr(), sw.data_ptr(),
                                                        N, K, s_ptr))
             del w
+            qa = self.qa_full[:, self.k0:self.k1].contiguous()
+            qw = qw[:, self.k0:self.k1].contiguous()
             out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             self.sets.append((qa, sa, qw, sw, out))
+        if world > 1:
+            self.scaling = "strong"
         self.i = 0
 
     def _outlier_x(self, T, D):
@@ -412,6 +448,10 @@ class GemmFP8(Workload):
         return x
 
     def _launch(self, qa, sa, qw, sw, out):
+        if self.world > 1:   # K-shard partial, then the bf16 sum over the ranks
+            import tp
+            tp.row_parallel_fp8(qa, sa, qw, sw, out)
+            return
         self.kc_lib.check(self.l.kc_gemm_fp8(qa.data_ptr(), sa.data_ptr(), qw.data_ptr(),
                                              sw.data_ptr(), out.data_ptr(), 0, self.M, self.N,
                                              self.K, self.N, self.s_ptr))
@@ -421,7 +461,13 @@ class GemmFP8(Workload):
         self.i += 1
 
     def work_per_step(self):
-        return 2.0 * self.M * self.N * self.K
+        return 2.0 * self.M * self.N * (self.k1 - self.k0)
+
+    def parallelism(self):
+        if self.world == 1:
+            return "single GPU"
+        return (f"row parallel x{self.world}: K/{self.world} code columns per GPU (scales from "
+                "full rows), bf16 partials summed by an NCCL all-reduce on the same stream")
 
     def config(self):
         return {"workload": "fp8-w8a8-gemm-4096x8192x8192", "M": self.M, "N": self.N,
@@ -438,9 +484,13 @@ class GemmFP8(Workload):
     def e2e_step(self):
         qa, sa, qw, sw, out = self.sets[0]
         self.x32.copy_(self.h_x, non_blocking=True)
-        self.kc_lib.check(self.l.kc_quantize_fp8_per_token(self.x32.data_ptr(), qa.data_ptr(),
-                                                           sa.data_ptr(), self.M, self.K,
-                                                           self.s_ptr))
+        self.kc_lib.check(self.l.kc_quantize_fp8_per_token(self.x32.data_ptr(),
+                                                           self.qa_full.data_ptr(), sa.data_ptr(),
+                                                           self.M, self.K, self.s_ptr))
+        if self.world > 1:
+            qa.copy_(self.qa_full[:, self.k0:self.k1])
+        else:
+            qa = self.qa_full
         self._launch(qa, sa, qw, sw, out)
         self.h_out.copy_(out, non_blocking=True)
 
@@ -476,8 +526,8 @@ class QuantFP8(Workload):
     profile = "quant_fp8_rows_8192x8192"
     T, D = 8192, 8192
 
-    def __init__(self, torch, l, dev, s_ptr, rank):
-        super().__init__(torch, l, dev, s_ptr, rank)
+    def __init__(self, torch, l, dev, s_ptr, rank, world=1):
+        super().__init__(torch, l, dev, s_ptr, rank, world)
         import kc_lib
         self.kc_lib = kc_lib
         x = torch.randn(self.T, self.D, device=dev, generator=self.gen)
@@ -542,8 +592,8 @@ class GemvInt4(Workload):
     R = C = 4096
     COPIES = 32   # 32 x 9 MB = 288 MB of distinct weights rotate through L2
 
-    def __init__(self, torch, l, dev, s_ptr, rank):
-        super().__init__(torch, l, dev, s_ptr, rank)
+    def __init__(self, torch, l, dev, s_ptr, rank, world=1):
+        super().__init__(torch, l, dev, s_ptr, rank, world)
         import kc_lib
         self.kc_lib = kc_lib
         R, C = self.R, self.C
@@ -677,7 +727,8 @@ def main(argv=None) -> int:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     dev = torch.device("cuda", torch.cuda.current_device())
     l = lib()
     stream = torch.cuda.current_stream()
@@ -685,9 +736,9 @@ def main(argv=None) -> int:
 
     W = WORKLOADS[args.workload]
     if W is GemvW4A16:
-        wl = W(torch, l, dev, s_ptr, rank, layers=args.layers)
+        wl = W(torch, l, dev, s_ptr, rank, world, layers=args.layers)
     else:
-        wl = W(torch, l, dev, s_ptr, rank)
+        wl = W(torch, l, dev, s_ptr, rank, world)
     torch.cuda.synchronize()
 
     for _ in range(args.warmup):
@@ -770,11 +821,11 @@ def main(argv=None) -> int:
 
     if rank == 0:
         cfg = wl.config()
-        cfg["parallelism"] = f"replicas x{world}"
+        cfg["parallelism"] = wl.parallelism()
         line = {
             "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
             "data": wl.data, "config": cfg,
             "roofline": {"bound": bound, "achieved": round(per_gpu, 1), "peak": peak,
                          "unit": unit, "frac": round(per_gpu / peak, 4), "peak_source": psrc,

@@ -10,7 +10,8 @@
  * reported through kc_get_last_error().
  *
  * Part 2 is the new kc_* API: int status (KC_OK == 0), never synchronizes
- * unless stated, never allocates device memory.  It carries the bf16 / fp16 /
+ * unless stated, never allocates device memory (kc_ipc_alloc, whose purpose
+ * is to allocate a shareable buffer, excepted).  It carries the bf16 / fp16 /
  * FP8 entry points the reference does not have (batched W4A16 GEMV, tcgen05
  * GEMMs, bf16 collectives, sharded drivers).
  *
@@ -257,6 +258,24 @@ KC_API int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const ui
                          void* out, int out_f32, int M, int N, int K, int group_size, int ldc,
                          cudaStream_t stream);
 
+/* Column-parallel W4A16 GEMM fused with the all-gather of its output (one
+ * process per GPU; no counterpart kernel in the reference, whose
+ * launch_col_parallel_linear + launch_allgather_nccl, tensor_parallel.cu:209 and
+ * tensor_parallel_nccl.cu:127, run the two steps apart).  This rank multiplies
+ * x [M, K] by its weight shard (rows rank*N_shard .. +N_shard of the full
+ * [N_shard*nranks, K] matrix, same packing as kc_gemm_w4a16) and its epilogue
+ * writes every bf16 tile straight into columns rank*N_shard .. of all nranks
+ * output buffers outs[r] ([M, N_shard*nranks] row-major bf16, 16-byte aligned;
+ * outs[rank] local, the others mapped peer memory, kc_ipc_open) over NVLink.
+ * Asynchronous: the caller synchronizes the ranks (e.g. a collective on the
+ * same stream) before reading the result, and before the next call if a rank
+ * may still be reading the previous one.  nranks <= KC_MAX_RANKS, N_shard % 32 == 0. */
+#define KC_MAX_RANKS 8
+KC_API int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed_shard,
+                                   const uint16_t* scales_shard, void* const* outs, int nranks,
+                                   int rank, int M, int N_shard, int K, int group_size,
+                                   cudaStream_t stream);
+
 /* fp32 C[M,N] = A[M,K] * B[N,K]^T (the column/row-parallel shard GEMM). */
 KC_API int kc_sgemm_nt(const float* A, const float* B, float* C, int M, int N, int K,
                 cudaStream_t stream);
@@ -283,6 +302,20 @@ KC_API int kc_allreduce_bf16(void* comm, const uint16_t* send, uint16_t* recv, l
                       cudaStream_t stream);
 KC_API int kc_allreduce_f32(void* comm, const float* send, float* recv, long count,
                      cudaStream_t stream);
+
+/* --- device buffers shared between the processes of one node (no reference
+ *     counterpart: the reference keeps every rank in one process) ------------- */
+/* Size in bytes of an opaque IPC handle. */
+KC_API int kc_ipc_handle_bytes(void);
+/* cudaMalloc'd buffer whose handle can be shared; free with kc_ipc_free after
+ * every peer closed its mapping. */
+KC_API int kc_ipc_alloc(void** dev_ptr, size_t bytes);
+KC_API int kc_ipc_free(void* dev_ptr);
+/* Handle of a kc_ipc_alloc buffer (kc_ipc_handle_bytes() bytes, host memory). */
+KC_API int kc_ipc_get_handle(const void* dev_ptr, void* handle_out);
+/* Maps a peer process's buffer into this process (peer access enabled). */
+KC_API int kc_ipc_open(const void* handle, void** dev_ptr);
+KC_API int kc_ipc_close(void* dev_ptr);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -55,10 +55,13 @@ constexpr uint32_t kACol = 256;           // A ring columns [256, 384)
 struct alignas(64) Params {
     CUtensorMap xmap;   // activations bf16 {K, M}, box {64, 256}, 128-byte swizzle
     CUtensorMap wmap;   // packed weights u8 {K/2, N}, box {32, 128}
-    CUtensorMap omap;   // output bf16 {N, M} (pitch ldc), box {32, 256}; valid if tma_out
+    CUtensorMap omap[KC_MAX_RANKS];  // output bf16 {N_out, M} (pitch ldc), box {32, 256}, one
+                                     // per destination buffer; valid if tma_out
     const __half* scales;
     void* out;
     int M, N, K, gs, ldc, out_f32, tma_out;
+    int ndst;      // destination buffers of each tile (1, or the ranks of an all-gather)
+    int col_off;   // first output column of this launch's N rows in every destination
     int tiles_w, tiles_t;
     uint32_t magic;     // 0x3F800000 (1.0f), kept in a register
     uint32_t gs_recip;      // ceil(2^32 / gs): k / gs == umulhi(k, gs_recip) for k * gs < 2^32
@@ -288,7 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
                 sm100::fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0 && n0 + q * 32 < P.N) {
-                    sm100::tma_store_2d(&P.omap, stage, n0 + q * 32, m0);
+                    for (int d = 0; d < P.ndst; ++d)   // local buffer, or every rank's (NVLink)
+                        sm100::tma_store_2d(&P.omap[d], stage, P.col_off + n0 + q * 32, m0);
                     sm100::bulk_commit_group();
                 }
             } else {
@@ -331,22 +335,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
 
 KC_DEFINE_STATUS_READER(gemm_w4a16)
 
-extern "C" {
+namespace {
 
-int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
-                  void* out, int out_f32, int M, int N, int K, int group_size, int ldc,
-                  cudaStream_t stream) {
-    KC_REQUIRE(x_bf16 && packed && scales_f16 && out, KC_ERR_INVALID_ARG, "null pointer argument");
+// Shared launcher: outs[0..ndst) each receive columns [col_off, col_off + N)
+// of the product (bf16 through the TMA-store epilogue when tma_out), or, for a
+// single destination, fp32 / unaligned output through direct stores.
+int launch_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
+                      void* const* outs, int ndst, int col_off, int out_cols, int out_f32, int M,
+                      int N, int K, int group_size, int ldc, cudaStream_t stream) {
+    KC_REQUIRE(x_bf16 && packed && scales_f16 && outs && outs[0], KC_ERR_INVALID_ARG,
+               "null pointer argument");
     KC_REQUIRE(M >= 0 && N >= 0 && K >= 0, KC_ERR_INVALID_ARG, "negative size");
     if (M == 0 || N == 0) return KC_OK;
     KC_REQUIRE(K > 0 && K % BK == 0, KC_ERR_INVALID_ARG, "K=%d must be a positive multiple of %d", K, BK);
     KC_REQUIRE(group_size > 0 && group_size % BK == 0 && K % group_size == 0, KC_ERR_INVALID_ARG,
                "group_size=%d must be a multiple of %d dividing K=%d", group_size, BK, K);
-    KC_REQUIRE(ldc >= N, KC_ERR_INVALID_ARG, "ldc=%d < N=%d", ldc, N);
+    KC_REQUIRE(ldc >= out_cols, KC_ERR_INVALID_ARG, "ldc=%d < output columns %d", ldc, out_cols);
     KC_REQUIRE((uint64_t)K * (uint64_t)group_size < (1ull << 32), KC_ERR_INVALID_ARG,
                "K * group_size must be below 2^32");
     KC_REQUIRE(kc::aligned(x_bf16, 16) && kc::aligned(packed, 16) && kc::aligned(scales_f16, 2) &&
-                   kc::aligned(out, 4),
+                   kc::aligned(outs[0], 4),
                KC_ERR_ALIGNMENT, "x and packed must be 16-byte aligned");
     Params P{};
     int st = kc::encode_2d(&P.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x_bf16, (uint64_t)K, (uint64_t)M,
@@ -355,14 +363,23 @@ int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t*
     st = kc::encode_2d(&P.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, packed, (uint64_t)(K / 2), (uint64_t)N,
                        (uint64_t)(K / 2), BK / 2, BW, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
-    P.tma_out = (!out_f32 && kc::aligned(out, 16) && ldc % 8 == 0) ? 1 : 0;
+    bool aligned = true;
+    for (int d = 0; d < ndst; ++d) aligned = aligned && outs[d] && kc::aligned(outs[d], 16);
+    P.tma_out = (!out_f32 && aligned && ldc % 8 == 0) ? 1 : 0;
+    KC_REQUIRE(ndst == 1 || P.tma_out, KC_ERR_ALIGNMENT,
+               "all-gather outputs must be bf16, 16-byte aligned, with a pitch divisible by 8");
     if (P.tma_out) {
-        st = kc::encode_2d(&P.omap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, (uint64_t)N, (uint64_t)M,
-                           (uint64_t)ldc * 2, 32, BT, CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (st) return st;
+        for (int d = 0; d < ndst; ++d) {
+            st = kc::encode_2d(&P.omap[d], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, outs[d],
+                               (uint64_t)out_cols, (uint64_t)M, (uint64_t)ldc * 2, 32, BT,
+                               CU_TENSOR_MAP_SWIZZLE_NONE);
+            if (st) return st;
+        }
     }
+    P.ndst = ndst;
+    P.col_off = col_off;
     P.scales = reinterpret_cast<const __half*>(scales_f16);
-    P.out = out;
+    P.out = outs[0];
     P.M = M;
     P.N = N;
     P.K = K;
@@ -380,6 +397,33 @@ int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t*
     const int tiles = P.tiles_w * P.tiles_t;
     gemm_w4a16_kernel<<<std::min(tiles, kc::sm_count()), kThreads, smem, stream>>>(P);
     return kc::check_launch("gemm_w4a16");
+}
+
+}  // namespace
+
+extern "C" {
+
+int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
+                  void* out, int out_f32, int M, int N, int K, int group_size, int ldc,
+                  cudaStream_t stream) {
+    void* outs[1] = {out};
+    return launch_gemm_w4a16(x_bf16, packed, scales_f16, outs, 1, 0, N, out_f32, M, N, K,
+                             group_size, ldc, stream);
+}
+
+int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed_shard,
+                            const uint16_t* scales_shard, void* const* outs, int nranks, int rank,
+                            int M, int N_shard, int K, int group_size, cudaStream_t stream) {
+    KC_REQUIRE(outs != nullptr && nranks >= 1 && nranks <= KC_MAX_RANKS && rank >= 0 &&
+                   rank < nranks,
+               KC_ERR_INVALID_ARG, "rank %d of %d outside 0..%d", rank, nranks, KC_MAX_RANKS - 1);
+    KC_REQUIRE(N_shard >= 0 && N_shard % 32 == 0, KC_ERR_INVALID_ARG,
+               "N_shard=%d must be a multiple of 32 (a store box never crosses into a peer's columns)",
+               N_shard);
+    const long cols = (long)N_shard * nranks;
+    KC_REQUIRE(cols < (1L << 31), KC_ERR_INVALID_ARG, "output too wide");
+    return launch_gemm_w4a16(x_bf16, packed_shard, scales_shard, outs, nranks, rank * N_shard,
+                             (int)cols, 0, M, N_shard, K, group_size, (int)cols, stream);
 }
 
 }  // extern "C"

@@ -30,6 +30,7 @@ KC_ERR_NCCL = 4
 KC_ERR_UNSUPPORTED = 5
 KC_ERR_TIMEOUT = 6
 KC_W4A16_MAX_PROBLEMS = 8
+KC_MAX_RANKS = 8
 
 
 class KcError(RuntimeError):
@@ -89,6 +90,13 @@ _PROTOS = [
     ("kc_sgemm_nt", ci, [vp, vp, vp, ci, ci, ci, vp]),
     ("kc_gemm_fp8", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, vp]),
+    ("kc_gemm_w4a16_allgather", ci, [vp, vp, vp, ctypes.POINTER(vp), ci, ci, ci, ci, ci, ci, vp]),
+    ("kc_ipc_handle_bytes", ci, []),
+    ("kc_ipc_alloc", ci, [ctypes.POINTER(vp), ctypes.c_size_t]),
+    ("kc_ipc_free", ci, [vp]),
+    ("kc_ipc_get_handle", ci, [vp, vp]),
+    ("kc_ipc_open", ci, [vp, ctypes.POINTER(vp)]),
+    ("kc_ipc_close", ci, [vp]),
     ("kc_nccl_unique_id_bytes", ci, []),
     ("kc_nccl_get_unique_id", ci, [vp]),
     ("kc_nccl_comm_init_rank", ci, [vp, ci, vp, ci]),

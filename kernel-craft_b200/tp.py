@@ -1,0 +1,178 @@
+"""tp -- tensor-parallel drivers of the quantized-linear GEMMs, one process per GPU.
+
+Mirrors the two sharded linears of kernel-craft's tensor_parallel.cu for the
+quantized GEMMs, with the processes of one node as ranks (the reference runs
+every rank inside one process, tensor_parallel.cu:209-243 and
+tensor_parallel_nccl.cu:105-135):
+
+* column parallel (``launch_col_parallel_linear`` + ``launch_allgather_nccl``):
+  rank r owns weight rows [r*N/R, (r+1)*N/R) of a W4A16 matrix; the activations
+  are replicated.  ``ColParallelW4A16`` runs the fused kernel
+  ``kc_gemm_w4a16_allgather``: its epilogue writes every output tile straight
+  into all ranks' [M, N] buffers over NVLink, so the all-gather costs no
+  separate pass and the result lands in [M, N] order (the reference gathers
+  rank-major blocks).
+* row parallel (``launch_row_parallel_linear`` + ``launch_ring_allreduce_nccl``):
+  rank r owns columns [r*K/R, (r+1)*K/R) of the FP8 codes of both operands (the
+  per-token and per-channel scales come from the full rows, so each partial
+  already carries the scale epilogue, which is linear); ``row_parallel_fp8``
+  runs ``kc_gemm_fp8`` on the shard and sums the bf16 partials with an NCCL
+  all-reduce on the same stream.
+
+The process group must be NCCL for the GPU collectives; every rank calls the
+same functions in the same order.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Tuple
+
+import torch
+import torch.distributed as dist
+
+import kc_lib
+from kc_lib import check, lib
+
+
+def shard_range(total: int, world: int, rank: int) -> Tuple[int, int]:
+    """[begin, end) of rank's equal share of `total`; `total` must divide evenly."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a world of {world}")
+    if total % world:
+        raise ValueError(f"{total} does not split evenly over {world} ranks")
+    share = total // world
+    return rank * share, (rank + 1) * share
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def barrier_on_stream(group=None) -> None:
+    """Stream-ordered barrier: a one-element all-reduce on the current stream,
+    so work queued after it on any rank starts only when every rank's
+    preceding work has finished."""
+    flag = torch.zeros(1, dtype=torch.float32, device="cuda")
+    dist.all_reduce(flag, group=group)
+
+
+class PeerBuffers:
+    """One device buffer per rank, every rank mapping every other rank's buffer
+    (CUDA IPC through the kc_ipc_* entry points; handles travel over the
+    process group).  ``ptrs[r]`` is rank r's buffer as seen from this process;
+    ``local`` wraps this rank's own buffer as a torch tensor view."""
+
+    def __init__(self, nbytes: int, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > kc_lib.KC_MAX_RANKS:
+            raise ValueError(f"at most {kc_lib.KC_MAX_RANKS} ranks")
+        l = lib()
+        own = ctypes.c_void_p()
+        check(l.kc_ipc_alloc(ctypes.byref(own), nbytes))
+        self._own = own
+        hb = l.kc_ipc_handle_bytes()
+        handle = (ctypes.c_char * hb)()
+        check(l.kc_ipc_get_handle(own, handle))
+        handles: List[bytes] = [b""] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.ptrs: List[int] = []
+        self._opened: List[ctypes.c_void_p] = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(own.value)
+                continue
+            p = ctypes.c_void_p()
+            check(l.kc_ipc_open(ctypes.create_string_buffer(h, hb), ctypes.byref(p)))
+            self._opened.append(p)
+            self.ptrs.append(p.value)
+        self.nbytes = nbytes
+
+    def local(self, shape, dtype) -> torch.Tensor:
+        """This rank's buffer as a CUDA tensor (no copy; valid until close())."""
+        n = 1
+        for d in shape:
+            n *= d
+        if n * torch.empty((), dtype=dtype).element_size() > self.nbytes:
+            raise ValueError("view larger than the buffer")
+        return _from_blob(self._own.value, shape, dtype, torch.cuda.current_device())
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers, waits for every rank, frees our own."""
+        l = lib()
+        for p in self._opened:
+            l.kc_ipc_close(p)
+        self._opened = []
+        dist.barrier(group=self.group)
+        if self._own:
+            l.kc_ipc_free(self._own)
+            self._own = ctypes.c_void_p()
+
+
+def _from_blob(ptr: int, shape, dtype, device: int) -> torch.Tensor:
+    """A tensor viewing device memory owned elsewhere (lifetime managed by the
+    caller), through the __cuda_array_interface__ protocol."""
+    typestr, view = {torch.bfloat16: ("<i2", torch.bfloat16), torch.float16: ("<f2", None),
+                     torch.float32: ("<f4", None), torch.uint8: ("|u1", None),
+                     torch.int8: ("|i1", None)}[dtype]
+
+    class _Blob:
+        __cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                    "data": (ptr, False), "version": 3, "strides": None}
+
+    t = torch.as_tensor(_Blob(), device=f"cuda:{device}")
+    return t.view(view) if view is not None else t
+
+
+class ColParallelW4A16:
+    """Column-parallel W4A16 linear with the fused all-gather.
+
+    Every rank holds the full activations x [M, K] (bf16) and its weight shard
+    (packed u8 [N/R, K/2], fp16 scales [N/R, K/gs]); ``__call__`` returns the
+    full bf16 output [M, N] in this rank's shared buffer, identical on every
+    rank once the call returns (the stream-ordered barrier is part of it)."""
+
+    def __init__(self, M: int, N: int, K: int, group_size: int = 128, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.M, self.N, self.K, self.gs = M, N, K, group_size
+        self.n_shard = N // self.world
+        shard_range(N, self.world, self.rank)  # validates the split
+        self.out_bufs = PeerBuffers(M * N * 2, group)
+        self.out = self.out_bufs.local((M, N), torch.bfloat16)
+        self._outs = (ctypes.c_void_p * self.world)(*self.out_bufs.ptrs)
+
+    def launch(self, x: torch.Tensor, packed_shard: torch.Tensor, scales_shard: torch.Tensor) -> None:
+        """The fused GEMM alone (no barrier): for timing and for callers that
+        synchronize the ranks themselves."""
+        check(lib().kc_gemm_w4a16_allgather(
+            ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(packed_shard.data_ptr()),
+            ctypes.c_void_p(scales_shard.data_ptr()), self._outs, self.world, self.rank, self.M,
+            self.n_shard, self.K, self.gs, _stream()))
+
+    def __call__(self, x, packed_shard, scales_shard) -> torch.Tensor:
+        # nobody may still read the previous result when the peers overwrite it
+        barrier_on_stream(self.group)
+        self.launch(x, packed_shard, scales_shard)
+        barrier_on_stream(self.group)
+        return self.out
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        self.out_bufs.close()
+
+
+def row_parallel_fp8(a_codes_shard: torch.Tensor, sa: torch.Tensor, w_codes_shard: torch.Tensor,
+                     sw: torch.Tensor, out: torch.Tensor, comm_group=None) -> torch.Tensor:
+    """Row-parallel FP8 linear: out [M, N] bf16 = sum over ranks of
+    (a_shard . w_shard^T) * sa[m] * sw[n], the partial of this rank computed by
+    kc_gemm_fp8 into `out` and summed in place by an NCCL all-reduce."""
+    M, Kr = a_codes_shard.shape
+    N = w_codes_shard.shape[0]
+    check(lib().kc_gemm_fp8(ctypes.c_void_p(a_codes_shard.data_ptr()), ctypes.c_void_p(sa.data_ptr()),
+                            ctypes.c_void_p(w_codes_shard.data_ptr()), ctypes.c_void_p(sw.data_ptr()),
+                            ctypes.c_void_p(out.data_ptr()), 0, M, N, Kr, out.stride(0), _stream()))
+    dist.all_reduce(out, group=comm_group)
+    return out

@@ -335,8 +335,10 @@ class GemmW4A16(Workload):
         self.i = 0
 
     def _launch(self, x, p, s, out):
-        if self.col is not None:   # fused GEMM + all-gather, stream barriers around it
-            self.col(x, p, s)
+        if self.col is not None:   # fused GEMM + all-gather, then a stream barrier
+            # back-to-back steps read nothing in between: the previous step's
+            # exit barrier already orders the overwrite
+            self.col(x, p, s, entry_barrier=False)
             return
         self.kc_lib.check(self.l.kc_gemm_w4a16(x.data_ptr(), p.data_ptr(), s.data_ptr(),
                                                out.data_ptr(), 0, self.M, self.N, self.K, GROUP,
@@ -354,7 +356,7 @@ class GemmW4A16(Workload):
             return "single GPU"
         return (f"column parallel x{self.world}: N/{self.world} weight rows per GPU, "
                 "output tiles stored into every GPU's [M, N] buffer by the GEMM epilogue "
-                "over NVLink (fused all-gather), stream barrier (NCCL) before and after")
+                "over NVLink (fused all-gather), one stream barrier (NCCL) per step")
 
     def config(self):
         return {"workload": "w4a16-gemm-2048x28672x8192", "M": self.M, "N": self.N, "K": self.K,
@@ -741,18 +743,27 @@ def main(argv=None) -> int:
         wl = W(torch, l, dev, s_ptr, rank, world)
     torch.cuda.synchronize()
 
+    t_w = time.perf_counter()
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
+    # heat phase: a step COUNT every rank agrees on (steps may contain
+    # collectives, so all ranks must run the same number of them)
+    per_step = (time.perf_counter() - t_w) / args.warmup
+    if world > 1:
+        t = torch.tensor([per_step], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        per_step = float(t.item())
+    heat_steps = int(min(args.heat_s / max(per_step, 1e-6), 20000))
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     sampler = ClockSampler(vis.split(",")[local].strip() if vis else str(local))
     sampler.start()
-    t_heat = time.perf_counter()
-    while time.perf_counter() - t_heat < args.heat_s:
-        for _ in range(4):
-            wl.step()
-        torch.cuda.synchronize()
+    for i in range(heat_steps):
+        wl.step()
+        if i % 8 == 7:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
 
     # ---- timed region ------------------------------------------------------
     if world > 1:

@@ -269,7 +269,7 @@ KC_API int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const ui
  * outs[rank] local, the others mapped peer memory, kc_ipc_open) over NVLink.
  * Asynchronous: the caller synchronizes the ranks (e.g. a collective on the
  * same stream) before reading the result, and before the next call if a rank
- * may still be reading the previous one.  nranks <= KC_MAX_RANKS, N_shard % 32 == 0. */
+ * may still be reading the previous one.  nranks <= KC_MAX_RANKS, N_shard % 128 == 0. */
 #define KC_MAX_RANKS 8
 KC_API int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed_shard,
                                    const uint16_t* scales_shard, void* const* outs, int nranks,

@@ -47,7 +47,7 @@ constexpr int kWBytes = BW * BK / 2;      // 4 KB packed weights per stage
 constexpr int kConvWarps = 8;
 constexpr int kEpiWarp0 = 2 + kConvWarps;            // warps 10..13
 constexpr int kThreads = (kEpiWarp0 + 4) * 32;       // 448
-constexpr int kStageBytes = BT * 32 * 2;             // 16 KB bf16 staging per epilogue warp
+constexpr int kStageBytes = BT * BW * 2;             // 64 KB bf16 output tile staging
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCol = 0;           // accumulator columns [0, 256)
 constexpr uint32_t kACol = 256;           // A ring columns [256, 384)
@@ -55,7 +55,7 @@ constexpr uint32_t kACol = 256;           // A ring columns [256, 384)
 struct alignas(64) Params {
     CUtensorMap xmap;   // activations bf16 {K, M}, box {64, 256}, 128-byte swizzle
     CUtensorMap wmap;   // packed weights u8 {K/2, N}, box {32, 128}
-    CUtensorMap omap[KC_MAX_RANKS];  // output bf16 {N_out, M} (pitch ldc), box {32, 256}, one
+    CUtensorMap omap[KC_MAX_RANKS];  // output bf16 {N_out, M} (pitch ldc), box {128, 256}, one
                                      // per destination buffer; valid if tma_out
     const __half* scales;
     void* out;
@@ -70,7 +70,7 @@ struct alignas(64) Params {
 struct Smem {
     uint8_t x[kStages][kXBytes];   // 1024-byte aligned (swizzle atoms)
     uint8_t w[kStages][kWBytes];
-    uint8_t stage[4][kStageBytes]; // epilogue tiles: [256 tokens][32 weight rows] bf16
+    uint8_t stage[kStageBytes];    // epilogue tile: [256 tokens][128 weight rows] bf16
     uint64_t full[kStages];        // activations + packed weights landed (tx)
     uint64_t empty[kStages];       // MMA (commit) and the stage's 4 converter warps done
     uint64_t afull[kStages];       // converters wrote the TMEM A stage
@@ -258,7 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
         // -------------------------------- epilogue --------------------------------
         const int q = warp & 3;
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-        uint8_t* stage = S.stage[q];
+        uint8_t* stage = S.stage;
+        const bool store_lead = warp == kEpiWarp0 && lane == 0;   // issues the tile's stores
         uint32_t t = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
             const int n0 = (tile / P.tiles_t) * BW, m0 = (tile % P.tiles_t) * BT;
@@ -266,9 +267,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
             sm100::mbar_wait_or_abort(&S.dfull, t & 1u, abort);
             sm100::tc_fence_after();
             if (P.tma_out) {
-                // the previous tile's TMA store has finished reading the staging tile
-                if (lane == 0) sm100::bulk_wait_group_read0();
-                __syncwarp();
+                // the previous tile's TMA stores have finished reading the staging tile
+                if (store_lead) sm100::bulk_wait_group_read0();
+                sm100::named_sync(1, 128);
 #pragma unroll 1
                 for (int c = 0; c < BT / 64; ++c) {
                     uint32_t r[32], r2[32];
@@ -281,18 +282,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
                         __syncwarp();
                         if (lane == 0) sm100::mbar_arrive(&S.dempty);
                     }
-                    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + c * 64 * 32 + lane;
+                    // row m of the tile holds its 128 weight rows: 256 bytes, of
+                    // which this warp writes its 32 (64 bytes, one per lane)
+                    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + c * 64 * BW + q * 32 + lane;
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        o[i * 32] = __float2bfloat16_rn(__uint_as_float(r[i]));
-                        o[(32 + i) * 32] = __float2bfloat16_rn(__uint_as_float(r2[i]));
+                        o[i * BW] = __float2bfloat16_rn(__uint_as_float(r[i]));
+                        o[(32 + i) * BW] = __float2bfloat16_rn(__uint_as_float(r2[i]));
                     }
                 }
                 sm100::fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0 && n0 + q * 32 < P.N) {
-                    for (int d = 0; d < P.ndst; ++d)   // local buffer, or every rank's (NVLink)
-                        sm100::tma_store_2d(&P.omap[d], stage, P.col_off + n0 + q * 32, m0);
+                sm100::named_sync(1, 128);   // all four strips are in the staging tile
+                if (store_lead) {
+                    // one 128-column box per destination: 256-byte rows, local
+                    // buffer or every rank's over NVLink
+                    for (int d = 0; d < P.ndst; ++d)
+                        sm100::tma_store_2d(&P.omap[d], stage, P.col_off + n0, m0);
                     sm100::bulk_commit_group();
                 }
             } else {
@@ -322,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
                 if (lane == 0) sm100::mbar_arrive(&S.dempty);
             }
         }
-        if (lane == 0) sm100::bulk_wait_group0();  // stores complete before the CTA exits
+        if (store_lead) sm100::bulk_wait_group0();  // stores complete before the CTA exits
     }
 
     sm100::tc_fence_before();
@@ -371,7 +376,7 @@ int launch_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint1
     if (P.tma_out) {
         for (int d = 0; d < ndst; ++d) {
             st = kc::encode_2d(&P.omap[d], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, outs[d],
-                               (uint64_t)out_cols, (uint64_t)M, (uint64_t)ldc * 2, 32, BT,
+                               (uint64_t)out_cols, (uint64_t)M, (uint64_t)ldc * 2, BW, BT,
                                CU_TENSOR_MAP_SWIZZLE_NONE);
             if (st) return st;
         }
@@ -417,9 +422,9 @@ int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed_shard,
     KC_REQUIRE(outs != nullptr && nranks >= 1 && nranks <= KC_MAX_RANKS && rank >= 0 &&
                    rank < nranks,
                KC_ERR_INVALID_ARG, "rank %d of %d outside 0..%d", rank, nranks, KC_MAX_RANKS - 1);
-    KC_REQUIRE(N_shard >= 0 && N_shard % 32 == 0, KC_ERR_INVALID_ARG,
-               "N_shard=%d must be a multiple of 32 (a store box never crosses into a peer's columns)",
-               N_shard);
+    KC_REQUIRE(N_shard >= 0 && N_shard % BW == 0, KC_ERR_INVALID_ARG,
+               "N_shard=%d must be a multiple of %d (a store box never crosses into a peer's columns)",
+               N_shard, BW);
     const long cols = (long)N_shard * nranks;
     KC_REQUIRE(cols < (1L << 31), KC_ERR_INVALID_ARG, "output too wide");
     return launch_gemm_w4a16(x_bf16, packed_shard, scales_shard, outs, nranks, rank * N_shard,

@@ -152,9 +152,13 @@ class ColParallelW4A16:
             ctypes.c_void_p(scales_shard.data_ptr()), self._outs, self.world, self.rank, self.M,
             self.n_shard, self.K, self.gs, _stream()))
 
-    def __call__(self, x, packed_shard, scales_shard) -> torch.Tensor:
-        # nobody may still read the previous result when the peers overwrite it
-        barrier_on_stream(self.group)
+    def __call__(self, x, packed_shard, scales_shard, entry_barrier: bool = True) -> torch.Tensor:
+        """entry_barrier: wait until no rank still reads the previous result
+        before the peers overwrite it; a caller whose ranks do nothing with the
+        output between calls (e.g. back-to-back calls, each ending in the exit
+        barrier) may skip it."""
+        if entry_barrier:
+            barrier_on_stream(self.group)
         self.launch(x, packed_shard, scales_shard)
         barrier_on_stream(self.group)
         return self.out

@@ -356,7 +356,7 @@ class GemmW4A16(Workload):
             return "single GPU"
         return (f"column parallel x{self.world}: N/{self.world} weight rows per GPU, "
                 "output tiles stored into every GPU's [M, N] buffer by the GEMM epilogue "
-                "over NVLink (fused all-gather), one stream barrier (NCCL) per step")
+                "over NVLink (fused all-gather), one peer-flag barrier per step")
 
     def config(self):
         return {"workload": "w4a16-gemm-2048x28672x8192", "M": self.M, "N": self.N, "K": self.K,
@@ -438,7 +438,10 @@ class GemmFP8(Workload):
             qw = qw[:, self.k0:self.k1].contiguous()
             out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             self.sets.append((qa, sa, qw, sw, out))
+        self.rp = None
         if world > 1:
+            import tp
+            self.rp = tp.RowParallelFP8(M, N, reduce=os.environ.get("KC_TP_REDUCE", "nccl"))
             self.scaling = "strong"
         self.i = 0
 
@@ -450,9 +453,8 @@ class GemmFP8(Workload):
         return x
 
     def _launch(self, qa, sa, qw, sw, out):
-        if self.world > 1:   # K-shard partial, then the bf16 sum over the ranks
-            import tp
-            tp.row_parallel_fp8(qa, sa, qw, sw, out)
+        if self.rp is not None:   # K-shard partial, then the bf16 sum over NVLink peers
+            self.rp(qa, sa, qw, sw, entry_barrier=False)
             return
         self.kc_lib.check(self.l.kc_gemm_fp8(qa.data_ptr(), sa.data_ptr(), qw.data_ptr(),
                                              sw.data_ptr(), out.data_ptr(), 0, self.M, self.N,
@@ -468,8 +470,11 @@ class GemmFP8(Workload):
     def parallelism(self):
         if self.world == 1:
             return "single GPU"
+        how = ("an NCCL all-reduce on the same stream" if self.rp.reduce == "nccl" else
+               "kc_allreduce_bf16_peer over NVLink peer memory (each GPU reduces 1/N of the "
+               "output in fp32 and writes it to every GPU) between two peer-flag barriers")
         return (f"row parallel x{self.world}: K/{self.world} code columns per GPU (scales from "
-                "full rows), bf16 partials summed by an NCCL all-reduce on the same stream")
+                f"full rows), bf16 partials summed by {how}")
 
     def config(self):
         return {"workload": "fp8-w8a8-gemm-4096x8192x8192", "M": self.M, "N": self.N,
@@ -494,7 +499,7 @@ class GemmFP8(Workload):
         else:
             qa = self.qa_full
         self._launch(qa, sa, qw, sw, out)
-        self.h_out.copy_(out, non_blocking=True)
+        self.h_out.copy_(self.rp.out if self.rp is not None else out, non_blocking=True)
 
     @classmethod
     def _cpu(cls, rows):

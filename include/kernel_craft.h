@@ -276,6 +276,30 @@ KC_API int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed
                                    int rank, int M, int N_shard, int K, int group_size,
                                    cudaStream_t stream);
 
+/* bf16 sum all-reduce over NVLink peer memory (one process per GPU; the
+ * reference's counterpart is launch_ring_allreduce_nccl, fp32,
+ * tensor_parallel_nccl.cu:105).  partials[r] / outs[r]: rank r's input and
+ * output buffers of `count` bf16 as mapped in this process (own buffer at
+ * index `rank`, peers' through kc_ipc_open).  This rank reduces the rank-th
+ * 1/nranks slice -- fp32 sum in rank order, one rounding -- and writes it into
+ * every outs[r]; all ranks together produce the full sum in every output.
+ * The kernel does not synchronize with its peers: every rank's partial must be
+ * complete before any rank launches, and the outputs are complete once every
+ * rank's launch has finished (order both with collectives on the stream).
+ * count % (8 * nranks) == 0, 16-byte aligned buffers, nranks <= KC_MAX_RANKS. */
+KC_API int kc_allreduce_bf16_peer(const void* const* partials, void* const* outs, int nranks,
+                                  int rank, long count, cudaStream_t stream);
+
+/* Stream-ordered barrier of the ranks of one node over peer memory (no
+ * reference counterpart).  flags[r]: rank r's array of KC_MAX_RANKS ints
+ * (zeroed once before first use; own array at index `rank`, peers' through
+ * kc_ipc_open).  Every rank calls it with the same, increasing epoch (> 0);
+ * one warp publishes the epoch to every rank and waits -- at most 2 s, then
+ * kc_get_device_status() reports KC_ERR_TIMEOUT -- until all ranks published
+ * it.  Work queued after it on the stream starts only when every rank's work
+ * queued before it has finished. */
+KC_API int kc_peer_barrier(int* const* flags, int nranks, int rank, int epoch, cudaStream_t stream);
+
 /* fp32 C[M,N] = A[M,K] * B[N,K]^T (the column/row-parallel shard GEMM). */
 KC_API int kc_sgemm_nt(const float* A, const float* B, float* C, int M, int N, int K,
                 cudaStream_t stream);

@@ -35,6 +35,7 @@ int read_device_status_gemv(bool clear);
 int read_device_status_selftest(bool clear);
 int read_device_status_gemm_fp8(bool clear);
 int read_device_status_gemm_w4a16(bool clear);
+int read_device_status_peer(bool clear);
 
 __host__ __device__ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 

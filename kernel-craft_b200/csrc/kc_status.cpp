@@ -62,7 +62,8 @@ int kc_get_device_status(void) {
         return kc::set_error(KC_ERR_CUDA, "kc_get_device_status: device synchronize failed");
     int st = KC_OK;
     for (int v : {kc::read_device_status_gemv(true), kc::read_device_status_selftest(true),
-                  kc::read_device_status_gemm_fp8(true), kc::read_device_status_gemm_w4a16(true)})
+                  kc::read_device_status_gemm_fp8(true), kc::read_device_status_gemm_w4a16(true),
+                  kc::read_device_status_peer(true)})
         if (st == KC_OK && v != KC_OK) st = v;
     if (st != KC_OK) kc::set_error(st, "a device-side wait gave up (status %d)", st);
     return st;

@@ -91,6 +91,8 @@ _PROTOS = [
     ("kc_gemm_fp8", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16_allgather", ci, [vp, vp, vp, ctypes.POINTER(vp), ci, ci, ci, ci, ci, ci, vp]),
+    ("kc_allreduce_bf16_peer", ci, [ctypes.POINTER(vp), ctypes.POINTER(vp), ci, ci, cl, vp]),
+    ("kc_peer_barrier", ci, [ctypes.POINTER(vp), ci, ci, ci, vp]),
     ("kc_ipc_handle_bytes", ci, []),
     ("kc_ipc_alloc", ci, [ctypes.POINTER(vp), ctypes.c_size_t]),
     ("kc_ipc_free", ci, [vp]),

@@ -15,9 +15,11 @@ tensor_parallel_nccl.cu:105-135):
 * row parallel (``launch_row_parallel_linear`` + ``launch_ring_allreduce_nccl``):
   rank r owns columns [r*K/R, (r+1)*K/R) of the FP8 codes of both operands (the
   per-token and per-channel scales come from the full rows, so each partial
-  already carries the scale epilogue, which is linear); ``row_parallel_fp8``
-  runs ``kc_gemm_fp8`` on the shard and sums the bf16 partials with an NCCL
-  all-reduce on the same stream.
+  already carries the scale epilogue, which is linear); ``RowParallelFP8``
+  runs ``kc_gemm_fp8`` on the shard and sums the bf16 partials with
+  ``kc_allreduce_bf16_peer`` over NVLink peer memory (each rank reduces one
+  slice from all partials and writes it to every rank); ``row_parallel_fp8``
+  is the same linear with an NCCL all-reduce instead.
 
 The process group must be NCCL for the GPU collectives; every rank calls the
 same functions in the same order.
@@ -54,6 +56,31 @@ def barrier_on_stream(group=None) -> None:
     preceding work has finished."""
     flag = torch.zeros(1, dtype=torch.float32, device="cuda")
     dist.all_reduce(flag, group=group)
+
+
+class PeerBarrier:
+    """Stream-ordered barrier over peer memory (kc_peer_barrier): a one-warp
+    kernel per rank exchanges an increasing epoch through flag arrays shared
+    with CUDA IPC; cheaper than a one-element NCCL collective."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.bufs = PeerBuffers(kc_lib.KC_MAX_RANKS * 4, group)
+        self.bufs.local((kc_lib.KC_MAX_RANKS,), torch.int32).zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=group)          # every flag array is zero before first use
+        self._flags = (ctypes.c_void_p * self.world)(*self.bufs.ptrs)
+        self.epoch = 0
+
+    def __call__(self) -> None:
+        self.epoch += 1
+        check(lib().kc_peer_barrier(self._flags, self.world, self.rank, self.epoch, _stream()))
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        self.bufs.close()
 
 
 class PeerBuffers:
@@ -115,7 +142,7 @@ def _from_blob(ptr: int, shape, dtype, device: int) -> torch.Tensor:
     caller), through the __cuda_array_interface__ protocol."""
     typestr, view = {torch.bfloat16: ("<i2", torch.bfloat16), torch.float16: ("<f2", None),
                      torch.float32: ("<f4", None), torch.uint8: ("|u1", None),
-                     torch.int8: ("|i1", None)}[dtype]
+                     torch.int8: ("|i1", None), torch.int32: ("<i4", None)}[dtype]
 
     class _Blob:
         __cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
@@ -143,6 +170,7 @@ class ColParallelW4A16:
         self.out_bufs = PeerBuffers(M * N * 2, group)
         self.out = self.out_bufs.local((M, N), torch.bfloat16)
         self._outs = (ctypes.c_void_p * self.world)(*self.out_bufs.ptrs)
+        self.barrier = PeerBarrier(group)
 
     def launch(self, x: torch.Tensor, packed_shard: torch.Tensor, scales_shard: torch.Tensor) -> None:
         """The fused GEMM alone (no barrier): for timing and for callers that
@@ -158,13 +186,69 @@ class ColParallelW4A16:
         output between calls (e.g. back-to-back calls, each ending in the exit
         barrier) may skip it."""
         if entry_barrier:
-            barrier_on_stream(self.group)
+            self.barrier()
         self.launch(x, packed_shard, scales_shard)
-        barrier_on_stream(self.group)
+        self.barrier()
         return self.out
 
     def close(self) -> None:
         torch.cuda.synchronize()
+        self.barrier.close()
+        self.out_bufs.close()
+
+
+class RowParallelFP8:
+    """Row-parallel FP8 linear with the sum done over NVLink peer memory.
+
+    Every rank holds its K shard of the activation and weight codes and the
+    full-row scales; ``__call__`` runs kc_gemm_fp8 into this rank's shared
+    bf16 partial buffer, then kc_allreduce_bf16_peer (each rank reduces its
+    1/R slice from all partials in fp32 and writes it into every rank's
+    output), with a peer-memory barrier before and after the reduction.
+    Returns this rank's [M, N] bf16 output buffer (the same on every rank)."""
+
+    def __init__(self, M: int, N: int, group=None, reduce: str = "peer"):
+        if reduce not in ("peer", "nccl"):
+            raise ValueError("reduce must be 'peer' or 'nccl'")
+        self.reduce = reduce
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.M, self.N = M, N
+        if (M * N) % (8 * self.world):
+            raise ValueError("M * N must be a multiple of 8 * world")
+        self.part_bufs = PeerBuffers(M * N * 2, group)
+        self.out_bufs = PeerBuffers(M * N * 2, group)
+        self.partial = self.part_bufs.local((M, N), torch.bfloat16)
+        self.out = self.out_bufs.local((M, N), torch.bfloat16)
+        self._parts = (ctypes.c_void_p * self.world)(*self.part_bufs.ptrs)
+        self._outs = (ctypes.c_void_p * self.world)(*self.out_bufs.ptrs)
+        self.barrier = PeerBarrier(group)
+
+    def __call__(self, a_codes_shard, sa, w_codes_shard, sw, entry_barrier: bool = True) -> torch.Tensor:
+        """entry_barrier: wait until no rank still reads the previous call's
+        partials or output; back-to-back calls whose ranks touch neither in
+        between may skip it (the previous exit barrier orders them)."""
+        Kr = a_codes_shard.shape[1]
+        l = lib()
+        if self.reduce == "nccl":   # GEMM into the local output, NCCL sums in place
+            return row_parallel_fp8(a_codes_shard, sa, w_codes_shard, sw, self.out, self.group)
+        if entry_barrier:
+            self.barrier()
+        check(l.kc_gemm_fp8(ctypes.c_void_p(a_codes_shard.data_ptr()), ctypes.c_void_p(sa.data_ptr()),
+                            ctypes.c_void_p(w_codes_shard.data_ptr()), ctypes.c_void_p(sw.data_ptr()),
+                            ctypes.c_void_p(self.partial.data_ptr()), 0, self.M, self.N, Kr, self.N,
+                            _stream()))
+        self.barrier()      # every partial is complete
+        check(l.kc_allreduce_bf16_peer(self._parts, self._outs, self.world, self.rank,
+                                       self.M * self.N, _stream()))
+        self.barrier()      # every slice is in every output
+        return self.out
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        self.barrier.close()
+        self.part_bufs.close()
         self.out_bufs.close()
 
 

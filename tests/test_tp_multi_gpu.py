@@ -4,8 +4,10 @@ Column parallel: the fused GEMM + all-gather (kc_gemm_w4a16_allgather) must
 give every rank the single-GPU kc_gemm_w4a16 result of the full problem bit
 for bit (each output tile is computed by one rank with the same arithmetic and
 stored, unchanged, into every rank's buffer).  Row parallel: the K-sharded FP8
-GEMM + bf16 NCCL all-reduce against the single-GPU FP8 GEMM, normwise <= 1e-2
-(bf16 partials are rounded before the sum).  Skipped with fewer than 2 GPUs.
+GEMM + bf16 sum -- by NCCL all-reduce and by the peer-memory kernel
+kc_allreduce_bf16_peer -- against the single-GPU FP8 GEMM, normwise <= 1e-2
+(bf16 partials are rounded before the sum); the peer sum is identical on
+every rank.  Skipped with fewer than 2 GPUs.
 """
 import datetime
 import os
@@ -64,13 +66,23 @@ def _rank_main(rank, world, port, out_dir):
         kc_lib.check(l.kc_gemm_fp8(qa.data_ptr(), sa.data_ptr(), qw.data_ptr(), sw.data_ptr(),
                                    ref.data_ptr(), 1, M2, N2, K2, N2, st))
         k0, k1 = tp.shard_range(K2, world, rank)
+        qa_s, qw_s = qa[:, k0:k1].contiguous(), qw[:, k0:k1].contiguous()
         out = torch.empty(M2, N2, dtype=torch.bfloat16, device="cuda")
-        tp.row_parallel_fp8(qa[:, k0:k1].contiguous(), sa, qw[:, k0:k1].contiguous(), sw, out)
+        tp.row_parallel_fp8(qa_s, sa, qw_s, sw, out)
         torch.cuda.synchronize()
         row_err = float((out.float() - ref).abs().max() / ref.abs().max())
+        rp = tp.RowParallelFP8(M2, N2)
+        y2 = rp(qa_s, sa, qw_s, sw)
+        torch.cuda.synchronize()
+        row_err = max(row_err, float((y2.float() - ref).abs().max() / ref.abs().max()))
+        # the peer reduction sums in fp32 once: every rank holds identical bits
+        gathered = [torch.empty_like(y2) for _ in range(world)]
+        dist.all_gather(gathered, y2.clone())
+        row_same = all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16)) for g in gathered)
+        rp.close()
         status = l.kc_get_device_status()
         np.save(os.path.join(out_dir, f"rank{rank}.npy"),
-                np.array([col_ok, row_err, status], dtype=np.float64))
+                np.array([col_ok, row_err, status, row_same], dtype=np.float64))
         col.close()
     finally:
         dist.destroy_process_group()
@@ -82,7 +94,8 @@ def test_tensor_parallel_two_gpus(tmp_path):
     import torch.multiprocessing as mp
     mp.spawn(_rank_main, args=(WORLD, _free_port(), str(tmp_path)), nprocs=WORLD, join=True)
     for r in range(WORLD):
-        col_ok, row_err, status = np.load(tmp_path / f"rank{r}.npy")
+        col_ok, row_err, status, row_same = np.load(tmp_path / f"rank{r}.npy")
+        assert row_same == 1.0, "peer all-reduce outputs differ between ranks"
         assert col_ok == 1.0, f"rank {r}: gathered W4A16 output differs from the single-GPU GEMM"
         assert row_err <= 1e-2, f"rank {r}: row-parallel FP8 error {row_err}"
         assert status == 0

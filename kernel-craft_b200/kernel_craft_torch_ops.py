@@ -19,8 +19,9 @@ Differences from the reference bridge, all on inputs the reference mishandles:
     non-synchronizing ``kc_*`` twins (results are ordered on the stream).
 
 New operators (no reference counterpart): ``w4a16_dequantize``,
-``w4a16_gemv``, ``w4a16_gemv_grouped``, ``fp8_quantize_per_channel``,
-``smoothquant_fp8_quantize``, ``smoothquant_scale``.
+``w4a16_gemv``, ``w4a16_gemv_grouped``, ``w4a16_gemm``, ``fp8_gemm``,
+``fp8_quantize_per_channel``, ``smoothquant_fp8_quantize``,
+``smoothquant_scale``.
 """
 from __future__ import annotations
 
@@ -199,6 +200,41 @@ def w4a16_gemv_grouped(problems: Sequence[Tuple[torch.Tensor, torch.Tensor, torc
     return outs
 
 
+def w4a16_gemm(x, packed, scales_f16, group_size: int = 128, out_dtype=torch.bfloat16):
+    """C[M, N] = x[M, K] (bf16) . W^T on the tcgen05 tensor cores, W the GPTQ W4
+    [N, K] (packed u8 [N, K/2], fp16 scales [N, K/gs]); fp32 accumulation,
+    bf16 (default) or fp32 output."""
+    x, packed, scales_f16 = x.contiguous(), packed.contiguous(), scales_f16.contiguous()
+    _require_cuda(x, packed, scales_f16)
+    m, k = x.shape
+    n = packed.shape[0]
+    if packed.shape[1] * 2 != k:
+        raise ValueError(f"x has K={k}, packed weights K={packed.shape[1] * 2}")
+    out = torch.empty(m, n, dtype=out_dtype, device=x.device)
+    with kernel_span("w4a16_gemm", rows=n, cols=k, batch=m, group_size=group_size):
+        check(lib().kc_gemm_w4a16(_ptr(x), _ptr(packed), _ptr(scales_f16), _ptr(out),
+                                  1 if out_dtype == torch.float32 else 0, m, n, k, group_size, n,
+                                  _stream()))
+    return out
+
+
+def fp8_gemm(a_codes, sa, w_codes, sw, out_dtype=torch.bfloat16):
+    """out[M, N] = (e4m3(a) . e4m3(w)^T) * sa[m] * sw[n] on the tcgen05 tensor
+    cores: a_codes [M, K] and w_codes [N, K] the int8 E4M3 bit patterns of
+    fp8_quantize(per_token=True) / fp8_quantize_per_channel, fp32 accumulation,
+    bf16 (default) or fp32 output."""
+    a_codes, w_codes = a_codes.contiguous(), w_codes.contiguous()
+    sa, sw = sa.contiguous(), sw.contiguous()
+    _require_cuda(a_codes, sa, w_codes, sw)
+    m, k = a_codes.shape
+    n = w_codes.shape[0]
+    out = torch.empty(m, n, dtype=out_dtype, device=a_codes.device)
+    with kernel_span("fp8_gemm", rows=n, cols=k, batch=m):
+        check(lib().kc_gemm_fp8(_ptr(a_codes), _ptr(sa), _ptr(w_codes), _ptr(sw), _ptr(out),
+                                1 if out_dtype == torch.float32 else 0, m, n, k, n, _stream()))
+    return out
+
+
 # ---------------------------------------------------------------------------
 # torch.library registration (kernel_craft_torch_ops.py:428-471)
 # ---------------------------------------------------------------------------
@@ -216,12 +252,16 @@ def _register_torch_library() -> None:
     libdef.define("w4a16_dequantize(Tensor packed, Tensor scales_f16, int group_size) -> Tensor")
     libdef.define("fp8_quantize_per_channel(Tensor w) -> (Tensor, Tensor)")
     libdef.define("smoothquant_fp8_quantize(Tensor x, Tensor smooth) -> (Tensor, Tensor)")
+    libdef.define("w4a16_gemm(Tensor x, Tensor packed, Tensor scales_f16, int group_size) -> Tensor")
+    libdef.define("fp8_gemm(Tensor a_codes, Tensor sa, Tensor w_codes, Tensor sw) -> Tensor")
     impl = torch.library.Library("kernel_craft", "IMPL")
     for name, fn in (("int4_dequantize", int4_dequantize), ("int4_gemv", int4_gemv),
                      ("fp8_quantize", fp8_quantize), ("fp8_dequantize", fp8_dequantize),
                      ("w4a16_gemv", w4a16_gemv), ("w4a16_dequantize", w4a16_dequantize),
                      ("fp8_quantize_per_channel", fp8_quantize_per_channel),
-                     ("smoothquant_fp8_quantize", smoothquant_fp8_quantize)):
+                     ("smoothquant_fp8_quantize", smoothquant_fp8_quantize),
+                     ("w4a16_gemm", lambda x, p, s, gs: w4a16_gemm(x, p, s, gs)),
+                     ("fp8_gemm", lambda a, sa, w, sw: fp8_gemm(a, sa, w, sw))):
         impl.impl(name, fn, "CUDA")
     globals()["_torch_lib_def"] = libdef
     globals()["_torch_lib_impl"] = impl

@@ -68,3 +68,19 @@ def test_fp8_gemm_rejects_bad_args(cuda):
         kc_lib.check(l.kc_gemm_fp8(ptr(b), ptr(b), ptr(b), ptr(b), ptr(b), 0, 4, 8, 24, 8, stream()))
     with pytest.raises(kc_lib.KcError):   # N not a multiple of 8
         kc_lib.check(l.kc_gemm_fp8(ptr(b), ptr(b), ptr(b), ptr(b), ptr(b), 0, 4, 12, 32, 12, stream()))
+
+
+def test_fp8_gemm_torch_op(cuda):
+    """kernel_craft_torch_ops.fp8_gemm (and its torch.ops registration) on codes
+    and scales from the library's own per-token / per-channel quantizers."""
+    import kernel_craft_torch_ops as ops
+    M, N, K = 200, 264, 2048
+    x = O.make_outlier_activations(M, K, seed=31)
+    w = O.make_weight_f32(N, K, seed=32)
+    qa, sa = ops.fp8_quantize(dev(x), per_token=True)
+    qw, sw = ops.fp8_quantize_per_channel(dev(w))
+    y = ops.fp8_gemm(qa, sa, qw, sw, out_dtype=torch.float32)
+    ref = O.gemm_fp8_rowcol(host(qa).view(np.uint8), host(sa), host(qw).view(np.uint8), host(sw))
+    assert normwise_err(host(y), ref) <= 1e-4
+    y2 = torch.ops.kernel_craft.fp8_gemm(qa, sa, qw, sw)
+    assert y2.dtype == torch.bfloat16 and normwise_err(host(y2.float()), ref) <= 1e-2

@@ -71,3 +71,20 @@ def test_w4a16_gemm_rejects_bad_args(cuda):
         kc_lib.check(l.kc_gemm_w4a16(ptr(b), ptr(b), ptr(b), ptr(b), 0, 4, 8, 192, 128, 8, stream()))
     with pytest.raises(kc_lib.KcError):   # misaligned activations
         kc_lib.check(l.kc_gemm_w4a16(ptr(b[2:]), ptr(b), ptr(b), ptr(b), 0, 4, 8, 128, 64, 8, stream()))
+
+
+def test_w4a16_gemm_torch_op(cuda):
+    """kernel_craft_torch_ops.w4a16_gemm and torch.ops.kernel_craft.w4a16_gemm
+    run the same kernel as the C ABI call."""
+    import kernel_craft_torch_ops as ops
+    M, N, K, gs = 300, 384, 1024, 128
+    packed, scales = O.make_w4_gptq(N, K, gs, seed=21)
+    x = O.make_activations_bf16(M, K, seed=22)
+    dx = dev(x.view(np.int16)).view(torch.bfloat16)
+    dp, ds = dev(packed), dev(scales)
+    y = ops.w4a16_gemm(dx, dp, ds, gs)
+    assert y.shape == (M, N) and y.dtype == torch.bfloat16
+    ref = _run(x, packed, scales, M, N, K, gs, out_f32=False)
+    np.testing.assert_array_equal(host(y.float()), ref)
+    y2 = torch.ops.kernel_craft.w4a16_gemm(dx, dp, ds, gs)
+    assert torch.equal(y2, y)

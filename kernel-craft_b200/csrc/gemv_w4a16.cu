@@ -5,18 +5,20 @@
 // x bf16, fp32 accumulation, fp32 y.  Several problems (e.g. the four
 // projections of a decoder layer) can share one launch.
 //
-// Work decomposition: 16-row tiles in problem-major order, persistent CTAs of
-// eight warps (two per SM); the warps of a CTA split a tile's K range into
-// contiguous runs of 128-k chunks (16 rows x 64 bytes = 1 KB each) and reduce
-// their partial sums through shared memory at the end of the tile.
+// Work decomposition: 16-row tiles in problem-major order, one persistent CTA
+// per SM holding two or three independent groups of eight warps (Shape); the
+// warps of a group split a tile's K range into contiguous runs of 128-k chunks
+// (16 rows x 64 bytes = 1 KB each) and reduce their partial sums through
+// shared memory at the end of the tile.
 //
-// Memory pipeline: every warp owns a ring of kRing stages in shared memory,
-// each holding up to four chunks ("a quad", 4 KB).  Its lane 0 issues the
-// quad's 2-D TMA loads (box 64 bytes x 16 rows; rows past N read as zero) on
-// the stage's mbarrier, running kRing quads ahead of the warp's compute,
-// across tile boundaries; a tile's fp16 scale block (16 contiguous rows)
-// arrives by one bulk copy per tile, issued a tile ahead.  One wait and one
-// issue per 4 KB keeps the per-chunk bookkeeping small.
+// Memory pipeline: every warp owns a ring of one or two stages in shared
+// memory, each holding up to four chunks ("a quad", 4 KB).  Its lane 0 issues
+// the quad's 2-D TMA loads (box 64 bytes x 16 rows; rows past N read as zero)
+// on the stage's mbarrier as soon as the stage is consumed, so the ring runs
+// ahead of the warp's compute across tile boundaries, and the 16-24 warps of
+// an SM keep 96-128 KB of weights in flight; a tile's fp16 scale block (16
+// contiguous rows) arrives by one bulk copy per tile, issued tiles ahead.
+// One wait and one issue per 4 KB keeps the per-chunk bookkeeping small.
 //
 // Compute: a lane (g = lane / 4, t = lane % 4) reads rows g and g + 8, 16
 // bytes each, of a chunk and turns every 32-bit word into four bf16x2 MMA
@@ -70,26 +72,37 @@ struct alignas(64) Params {
 };
 
 constexpr int kGroupWarps = 8;                    // warps that split one tile's K range
-constexpr int kGroups = 2;                        // independent tile groups per CTA
-constexpr int kWarps = kGroupWarps * kGroups;
-constexpr int kThreads = kWarps * 32;
 constexpr int kGroupThreads = kGroupWarps * 32;
 constexpr int kChunkBytes = 1024;                 // 16 rows x 64 bytes = 128 k
 constexpr int kQuad = 4;                          // chunks per stage
-constexpr int kRing = 2;                          // stages per warp
+
+// CTA shape per activation tile count.  NT = 1 (M <= 8): three tile groups
+// (24 warps) with one stage per warp -- more independent warps hide the
+// per-chunk latency better than a deeper per-warp ring (34.2 vs 36.1 us per
+// 7B layer at M = 1 on B200, 43.6 vs 47.5 at M = 4).  NT = 2 needs more
+// registers per thread than 24 warps leave (the unstaged form spills), so it
+// keeps two groups (16 warps) with two stages per warp.
+template <int NT>
+struct Shape {
+    static constexpr int groups = NT == 1 ? 3 : 2;  // independent tile groups per CTA
+    static constexpr int ring = NT == 1 ? 1 : 2;    // stages per warp
+    static constexpr int warps = kGroupWarps * groups;
+    static constexpr int threads = warps * 32;
+};
 constexpr int kScaleHalves = 16 * 128;            // 16 rows x up to 128 groups
 constexpr int kScaleBufs = 3;                     // scale blocks in flight per group
 
 template <int NT>
 struct Smem {
-    uint8_t ring[kWarps][kRing][kQuad][kChunkBytes];  // TMA destinations, 1024-byte aligned
-    __half scales[kGroups][kScaleBufs][kScaleHalves];
-    float red[kGroups][2][kGroupWarps][16][NT * 8 + 1];  // double-buffered by tile parity
-    uint64_t wfull[kWarps][kRing];
-    uint64_t sfull[kGroups][kScaleBufs];
-    uint64_t xfull;            // staged activations landed
-    int red_cnt[kGroups][2];   // warps that stored their partials for the slot's tile
-    int red_done[kGroups][2];  // group tile counter of the last tile reduced from the slot
+    using Sh = Shape<NT>;
+    uint8_t ring[Sh::warps][Sh::ring][kQuad][kChunkBytes];  // TMA destinations, 1024-byte aligned
+    __half scales[Sh::groups][kScaleBufs][kScaleHalves];
+    float red[Sh::groups][2][kGroupWarps][16][NT * 8 + 1];  // double-buffered by tile parity
+    uint64_t wfull[Sh::warps][Sh::ring];
+    uint64_t sfull[Sh::groups][kScaleBufs];
+    uint64_t xfull;                // staged activations landed
+    int red_cnt[Sh::groups][2];    // warps that stored their partials for the slot's tile
+    int red_done[Sh::groups][2];   // group tile counter of the last tile reduced from the slot
     // then, if staged: the chunk sums float[sx_chunks][NT * 8], and the
     // activations of every problem, row m of problem i at
     // xs_off(i) + m * (2K + 16) bytes (the pad spreads rows over the banks),
@@ -169,14 +182,15 @@ __device__ __forceinline__ void warp_chunks(int C, int w, int& begin, int& end) 
 
 // A warp's position in its own sequence of (tile, quad) work items.
 struct Cursor {
-    int tile, c, cend, pi;
+    int tile, c, cend, pi, step;
 };
 
-// Tiles of a group: vg, vg + G, vg + 2G, ... with vg = 2 * blockIdx + group
-// and G = 2 * gridDim (every (CTA, group) pair walks its own tile sequence).
+// Tiles of a group: vg, vg + G, vg + 2G, ... with vg = groups * blockIdx + group
+// and G = step = groups * gridDim (every (CTA, group) pair walks its own tile
+// sequence).
 __device__ __forceinline__ void cursor_settle(const Params& P, Cursor& cu, int warp) {
     while (cu.tile < P.total_tiles && cu.c >= cu.cend) {
-        cu.tile += kGroups * gridDim.x;
+        cu.tile += cu.step;
         if (cu.tile >= P.total_tiles) break;
         cu.pi = problem_index(P, cu.tile);
         warp_chunks(P.p[cu.pi].K >> 7, warp, cu.c, cu.cend);
@@ -282,7 +296,7 @@ __device__ __forceinline__ void chunk_mma(const uint4& WA, const uint4& WB, cons
 // consecutive threads of one warp, which read before any of them writes.
 template <int NT>
 __device__ __forceinline__ void permute_staged(const Params& P, uint8_t* xs, float* sx) {
-    constexpr int kCols = NT * 8;
+    constexpr int kCols = NT * 8, kThreads = Shape<NT>::threads;
     for (int i = threadIdx.x; i < P.sx_chunks * kCols; i += kThreads) sx[i] = 0.f;
     __syncthreads();
     for (int pi = 0; pi < P.count; ++pi) {
@@ -331,10 +345,11 @@ __device__ __forceinline__ void load_x(const __nv_bfloat16* const (&xrow)[NT],
 }
 
 template <int NT, bool XS>
-__global__ void __launch_bounds__(kThreads, 1) gemv_w4a16_kernel(const __grid_constant__ Params P) {
+__global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const __grid_constant__ Params P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     using SM = Smem<NT>;
     constexpr int kCols = NT * 8;
+    constexpr int kGroups = Shape<NT>::groups, kWarps = Shape<NT>::warps, kRing = Shape<NT>::ring;
     SM& S = *reinterpret_cast<SM*>(smem_raw);
     float* sx = reinterpret_cast<float*>(smem_raw + fixed_smem<NT>());
     uint8_t* xs = reinterpret_cast<uint8_t*>(sx + (size_t)P.sx_chunks * kCols);
@@ -372,6 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_w4a16_kernel(const __grid_co
     pf.tile = first;
     pf.c = pf.cend = 0;
     pf.pi = 0;
+    pf.step = stride;
     if (pf.tile < total) {
         pf.pi = problem_index(P, pf.tile);
         warp_chunks(P.p[pf.pi].K >> 7, gw, pf.c, pf.cend);
@@ -569,10 +585,10 @@ int launch_tc(const Params& P, size_t stage_bytes, cudaStream_t stream) {
     auto kern = gemv_w4a16_kernel<NT, XS>;
     KC_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "gemv_w4a16 shared-memory attribute");
-    const int groups = (P.total_tiles + kGroups - 1) / kGroups;
+    const int groups = (P.total_tiles + Shape<NT>::groups - 1) / Shape<NT>::groups;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)std::min(groups, kc::sm_count()));
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(Shape<NT>::threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     // programmatic dependent launch: this grid may be scheduled while the

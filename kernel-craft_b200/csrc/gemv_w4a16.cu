@@ -25,8 +25,8 @@
 // fragments holding 128 + u exactly (nibble OR-ed into the mantissa of bf16
 // 128.0; 3 shifts + 4 LOP3 per 8 weights), fed straight from registers into
 // mma.sync m16n8k16 (weights as A, activations as B).  Activations are
-// staged once per problem in shared memory in fragment order (k0 k4 k1 k5 k2
-// k6 k3 k7 per 8-block) when they fit, together with their per-chunk sums, and
+// staged once per CTA in shared memory in fragment order (k0 k4 k1 k5 k2 k6
+// k3 k7 per 8-block) when they fit, together with their per-chunk sums, and
 // the offset is removed per chunk as sum (u - 8) x = sum (128 + u) x -
 // 136 * sum x; otherwise they are read from global memory (L1-resident),
 // permuted with PRMT, and a second MMA with the constant fragment -136 removes
@@ -65,7 +65,6 @@ struct alignas(64) Params {
     int M;
     int gs;
     int gshift;      // group of 128-k chunk c is c >> gshift
-    int stage_bytes;   // staged activation bytes copied (all problems), 0 = not staged
     int sx_chunks;     // chunk rows of the staged activation sums (all problems)
     uint32_t magic;  // 0x43004300 = bf16x2 (128, 128), held in a register (see nib_or)
     uint32_t neg136; // 0xC308C308 = bf16x2 (-136, -136): the unstaged path's offset MMA fragment
@@ -100,13 +99,12 @@ struct Smem {
     float red[Sh::groups][2][kGroupWarps][16][NT * 8 + 1];  // double-buffered by tile parity
     uint64_t wfull[Sh::warps][Sh::ring];
     uint64_t sfull[Sh::groups][kScaleBufs];
-    uint64_t xfull;                // staged activations landed
     int red_cnt[Sh::groups][2];    // warps that stored their partials for the slot's tile
     int red_done[Sh::groups][2];   // group tile counter of the last tile reduced from the slot
     // then, if staged: the chunk sums float[sx_chunks][NT * 8], and the
     // activations of every problem, row m of problem i at
     // xs_off(i) + m * (2K + 16) bytes (the pad spreads rows over the banks),
-    // permuted in place to fragment order after they land
+    // in fragment order
 };
 
 template <int NT>
@@ -185,9 +183,9 @@ struct Cursor {
     int tile, c, cend, pi, step;
 };
 
-// Tiles of a group: vg, vg + G, vg + 2G, ... with vg = groups * blockIdx + group
-// and G = step = groups * gridDim (every (CTA, group) pair walks its own tile
-// sequence).
+// Tiles of a group: vg, vg + G, vg + 2G, ... with vg = blockIdx + group *
+// gridDim and G = step = groups * gridDim (every (CTA, group) pair walks its
+// own tile sequence).
 __device__ __forceinline__ void cursor_settle(const Params& P, Cursor& cu, int warp) {
     while (cu.tile < P.total_tiles && cu.c >= cu.cend) {
         cu.tile += cu.step;
@@ -288,43 +286,67 @@ __device__ __forceinline__ void chunk_mma(const uint4& WA, const uint4& WB, cons
             cm[nt][e] += XS ? c1[nt][e] : (c1[nt][e] + (o0[nt][e] + o1[nt][e]));
 }
 
-// In-place pass over the staged activations (natural order on arrival): each
-// 8-element block is permuted to fragment order, and within each 128-k chunk
-// the sixteen blocks b = 4t + j (k = 32t + 8j) move to position 4j + t, so a
-// lane's LDS.128 for word j hits 16 consecutive bytes per t.  The same pass
-// forms the per-chunk sums sx[c][m] (fp32).  A chunk's 16 blocks belong to 16
-// consecutive threads of one warp, which read before any of them writes.
+// Stages the activations of every problem: each 8-element block (16 bytes)
+// is loaded from global memory, permuted to fragment order, and within each
+// 128-k chunk the sixteen blocks b = 4t + j (k = 32t + 8j) move to position
+// 4j + t, so a lane's LDS.128 for word j hits 16 consecutive bytes per t.  The
+// same pass forms the per-chunk sums sx[c][m] (fp32): a chunk's 16 blocks
+// belong to 16 consecutive lanes of one warp.  Work is handed out in units of
+// 32 blocks, one per lane, and every warp loads U units before it processes
+// any, so the loads of a warp are in flight together.  Plain loads rather than
+// a bulk copy: a bulk copy queues behind the weight tiles the CTA has already
+// requested and lands later.
 template <int NT>
-__device__ __forceinline__ void permute_staged(const Params& P, uint8_t* xs, float* sx) {
-    constexpr int kCols = NT * 8, kThreads = Shape<NT>::threads;
-    for (int i = threadIdx.x; i < P.sx_chunks * kCols; i += kThreads) sx[i] = 0.f;
-    __syncthreads();
-    for (int pi = 0; pi < P.count; ++pi) {
-        const Prob& pr = P.p[pi];
-        const int nb = pr.K >> 3;                    // a multiple of 16
-        const int rounds = (nb + 31) & ~31;          // whole warps: the shuffles need every lane
-        for (int m = 0; m < P.M; ++m) {
-            uint8_t* row = xs + pr.xs_off + (size_t)m * (2 * pr.K + 16);
-            for (int kb = threadIdx.x; kb < rounds; kb += kThreads) {
-                const bool valid = kb < nb;
-                const uint4 v = valid ? *reinterpret_cast<const uint4*>(row + kb * 16) : make_uint4(0, 0, 0, 0);
-                float sum = 0.f;
-                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+__device__ __forceinline__ void stage_activations(const Params& P, uint8_t* xs, float* sx) {
+    constexpr int kCols = NT * 8, kThreads = Shape<NT>::threads, kW = kThreads / 32, U = 4;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // sums of columns m >= M stay zero (columns m < M are all written below)
+    for (int i = threadIdx.x; i < P.sx_chunks * kCols; i += kThreads)
+        if (i % kCols >= P.M) sx[i] = 0.f;
+    int total_units = 0;
+    for (int pi = 0; pi < P.count; ++pi) total_units += P.M * ((P.p[pi].K + 255) >> 8);
+    for (int u0 = warp; u0 < total_units; u0 += U * kW) {
+        uint4 v[U];
+        int pis[U], ms[U], kbs[U];
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    sum += __uint_as_float(w4[i] << 16) + __uint_as_float(w4[i] & 0xFFFF0000u);
-#pragma unroll
-                for (int o = 8; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                __syncwarp();   // the chunk's blocks are all read before any is rewritten
-                if (valid) {
-                    const int c = kb >> 4, r = kb & 15;
-                    const int pos = (c << 4) + ((r & 3) << 2) + (r >> 2);
-                    *reinterpret_cast<uint4*>(row + pos * 16) =
-                        make_uint4(prmt(v.x, v.z, 0x5410u), prmt(v.x, v.z, 0x7632u),
-                                   prmt(v.y, v.w, 0x5410u), prmt(v.y, v.w, 0x7632u));
-                    if (r == 0) sx[(pr.sx_off + c) * kCols + m] = sum;
+        for (int b = 0; b < U; ++b) {
+            int u = u0 + b * kW;
+            pis[b] = -1;
+            if (u < total_units) {
+                int pi = 0;
+                while (u >= P.M * ((P.p[pi].K + 255) >> 8)) {
+                    u -= P.M * ((P.p[pi].K + 255) >> 8);
+                    ++pi;
                 }
+                const int per = (P.p[pi].K + 255) >> 8;  // units per activation row
+                pis[b] = pi;
+                ms[b] = u / per;
+                kbs[b] = (u % per) * 32 + lane;
+                v[b] = kbs[b] < (P.p[pi].K >> 3)
+                           ? __ldcg(reinterpret_cast<const uint4*>(P.p[pi].x + (size_t)ms[b] * P.p[pi].K) +
+                                    kbs[b])
+                           : make_uint4(0, 0, 0, 0);
             }
+        }
+#pragma unroll
+        for (int b = 0; b < U; ++b) {
+            if (pis[b] < 0) break;  // warp-uniform
+            const Prob& pr = P.p[pis[b]];
+            float sum = 0.f;
+            const uint32_t w4[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                sum += __uint_as_float(w4[i] << 16) + __uint_as_float(w4[i] & 0xFFFF0000u);
+#pragma unroll
+            for (int o = 8; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            const int kb = kbs[b], c = kb >> 4, r = kb & 15;
+            if (kb >= (pr.K >> 3)) continue;  // past the row (K % 256 == 128)
+            uint8_t* row = xs + pr.xs_off + (size_t)ms[b] * (2 * pr.K + 16);
+            const int pos = (c << 4) + ((r & 3) << 2) + (r >> 2);
+            *reinterpret_cast<uint4*>(row + pos * 16) =
+                make_uint4(prmt(v[b].x, v[b].z, 0x5410u), prmt(v[b].x, v[b].z, 0x7632u),
+                           prmt(v[b].y, v[b].w, 0x5410u), prmt(v[b].y, v[b].w, 0x7632u));
+            if (r == 0) sx[(pr.sx_off + c) * kCols + ms[b]] = sum;
         }
     }
 }
@@ -359,7 +381,9 @@ __global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const
     const int g = lane >> 2, t = lane & 3;
     const int M = P.M, gshift = P.gshift, gs = P.gs, total = P.total_tiles;
     const uint32_t magic = P.magic, neg136 = P.neg136;
-    const int first = kGroups * blockIdx.x + group, stride = kGroups * gridDim.x;
+    // group-major: consecutive tiles (the longest-K ones first) go to different
+    // SMs before any SM gets a second one, which evens out the work per SM
+    const int first = blockIdx.x + group * gridDim.x, stride = kGroups * gridDim.x;
 
     // the next launch in the stream may start its prologue while this grid drains
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -371,7 +395,6 @@ __global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const
             S.red_cnt[h][0] = S.red_cnt[h][1] = 0;
             S.red_done[h][0] = S.red_done[h][1] = -1;
         }
-        sm100::mbar_init(&S.xfull, 1);
         sm100::fence_barrier_init();
     }
     __syncthreads();
@@ -402,18 +425,7 @@ __global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const
     // the activations (and y) may be produced / consumed by the previous grid
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if (XS) {
-        // one bulk copy per activation row, all landing on one barrier
-        if (threadIdx.x == 0) {
-            sm100::mbar_arrive_expect_tx(&S.xfull, (uint32_t)P.stage_bytes);
-            for (int i = 0; i < P.count; ++i) {
-                const Prob& q = P.p[i];
-                for (int m = 0; m < M; ++m)
-                    sm100::bulk_g2s(xs + q.xs_off + (size_t)m * (2 * q.K + 16), q.x + (size_t)m * q.K,
-                                    (uint32_t)(2 * q.K), &S.xfull);
-            }
-        }
-        sm100::mbar_wait(&S.xfull, 0);
-        permute_staged<NT>(P, xs, sx);
+        stage_activations<NT>(P, xs, sx);
         __syncthreads();
     }
     const uint32_t sx_base = sm100::smem_u32(sx) + 8 * t;  // columns 2t, 2t+1 (+8 nt)
@@ -646,19 +658,17 @@ int launch(Params& P, cudaStream_t stream) {
     }
     // stage every problem's activations when they all fit
     const int NT = P.M <= 8 ? 1 : 2;
-    long xs_bytes = 0, copied = 0, chunks = 0;  // padded footprint, bytes copied
+    long xs_bytes = 0, chunks = 0;  // padded footprint, chunk rows
     for (int i = 0; i < P.count; ++i) {
         Prob& q = P.p[i];
         q.xs_off = (int)xs_bytes;
         q.sx_off = (int)chunks;
         xs_bytes += (long)P.M * (2L * q.K + 16);
-        copied += (long)P.M * 2L * q.K;
         chunks += q.K / 128;
     }
     const size_t fixed = NT == 1 ? fixed_smem<1>() : fixed_smem<2>();
     const size_t sx_bytes = (size_t)chunks * NT * 8 * 4;
     const bool stage = fixed + sx_bytes + (size_t)xs_bytes <= kSmemLimit;
-    P.stage_bytes = stage ? (int)copied : 0;
     P.sx_chunks = stage ? (int)chunks : 0;
     const size_t stage_bytes = stage ? sx_bytes + (size_t)xs_bytes : 0;
     if (NT == 1)

@@ -28,9 +28,9 @@
 // staged once per CTA in shared memory in fragment order (k0 k4 k1 k5 k2 k6
 // k3 k7 per 8-block) when they fit, together with their per-chunk sums, and
 // the offset is removed per chunk as sum (u - 8) x = sum (128 + u) x -
-// 136 * sum x; otherwise they are read from global memory (L1-resident),
-// permuted with PRMT, and a second MMA with the constant fragment -136 removes
-// the offset.  The group scale multiplies the per-chunk result.  MMA columns
+// 136 * sum x (the MMA accumulator starts at -136 * sum x); otherwise they
+// are read from global memory (L1-resident), permuted with PRMT, and a second
+// MMA with the constant fragment -136 removes the offset.  The group scale multiplies the per-chunk result.  MMA columns
 // m >= M read a valid (clamped) activation row and are
 // discarded, so no lane predication is needed.
 //
@@ -101,7 +101,7 @@ struct Smem {
     uint64_t sfull[Sh::groups][kScaleBufs];
     int red_cnt[Sh::groups][2];    // warps that stored their partials for the slot's tile
     int red_done[Sh::groups][2];   // group tile counter of the last tile reduced from the slot
-    // then, if staged: the chunk sums float[sx_chunks][NT * 8], and the
+    // then, if staged: the chunk offsets float[sx_chunks][NT * 8], and the
     // activations of every problem, row m of problem i at
     // xs_off(i) + m * (2K + 16) bytes (the pad spreads rows over the banks),
     // in fragment order
@@ -190,7 +190,8 @@ __device__ __forceinline__ void cursor_settle(const Params& P, Cursor& cu, int w
     while (cu.tile < P.total_tiles && cu.c >= cu.cend) {
         cu.tile += cu.step;
         if (cu.tile >= P.total_tiles) break;
-        cu.pi = problem_index(P, cu.tile);
+        // tiles only move forward, so the problem index does too
+        while (cu.pi + 1 < P.count && cu.tile >= P.p[cu.pi + 1].tile_begin) ++cu.pi;
         warp_chunks(P.p[cu.pi].K >> 7, warp, cu.c, cu.cend);
     }
 }
@@ -232,19 +233,21 @@ __device__ __forceinline__ void issue_scales(const Params& P, int tile, __half* 
     const int pi = problem_index(P, tile);
     const Prob& pr = P.p[pi];
     const int row0 = (tile - pr.tile_begin) * 16;
-    const uint32_t bytes = (uint32_t)min(16, pr.N - row0) * (uint32_t)(pr.K / P.gs) * 2u;
+    const int G = P.gshift == 31 ? 1 : ((pr.K >> 7) >> P.gshift);  // K / gs
+    const uint32_t bytes = (uint32_t)min(16, pr.N - row0) * (uint32_t)G * 2u;
     sm100::mbar_arrive_expect_tx(bar, bytes);
-    sm100::bulk_g2s(dst, pr.scales + (size_t)row0 * (pr.K / P.gs), bytes, bar);
+    sm100::bulk_g2s(dst, pr.scales + (size_t)row0 * G, bytes, bar);
 }
 
 // One 128-k chunk of one lane: rows g, g+8 (words WA, WB), activations X.
-// Staged (XS): X is in fragment order (x0x4, x1x5, x2x6, x3x7 per 8-block) and
-// cm receives sum (128 + u) x; the offset is removed by the caller with the
-// chunk's activation sum.  Unstaged: X is in natural order (x0x1, x2x3, x4x5,
+// Staged (XS): X is in fragment order (x0x4, x1x5, x2x6, x3x7 per 8-block);
+// the caller seeds cm with -136 * sum x of the chunk, and the chunk's eight
+// MMAs add sum (128 + u) x into it in one chain, so cm leaves with
+// sum (u - 8) x (one chain needs no accumulator merge; the other warps of the
+// SM cover its latency).  Unstaged: X is in natural order (x0x1, x2x3, x4x5,
 // x6x7), paired with PRMT, and a second MMA with the constant fragment -136
-// removes the offset, so cm receives sum (u - 8) x.  The MMAs of a chunk feed
-// independent accumulators (per k half of each word, weights and offset
-// apart), so no MMA waits on the one before it.
+// removes the offset; those MMAs feed independent accumulators (per k half of
+// each word, weights and offset apart) that are merged at the end.
 template <int NT, bool XS>
 __device__ __forceinline__ void chunk_mma(const uint4& WA, const uint4& WB, const uint4 (&X)[NT][4],
                                           uint32_t magic, uint32_t neg136, float (&cm)[NT][4]) {
@@ -274,23 +277,24 @@ __device__ __forceinline__ void chunk_mma(const uint4& WA, const uint4& WB, cons
                     b0 = prmt(lo, hi, 0x5410u);
                     b1 = prmt(lo, hi, 0x7632u);
                 }
-                mma_16816(h ? c1[nt] : cm[nt], A[2 * h], B[2 * h], A[2 * h + 1], B[2 * h + 1], b0, b1);
+                mma_16816((h && !XS) ? c1[nt] : cm[nt], A[2 * h], B[2 * h], A[2 * h + 1], B[2 * h + 1], b0, b1);
                 if (!XS) mma_16816(h ? o1[nt] : o0[nt], neg136, neg136, neg136, neg136, b0, b1);
             }
         }
     }
+    if (!XS)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-            cm[nt][e] += XS ? c1[nt][e] : (c1[nt][e] + (o0[nt][e] + o1[nt][e]));
+            for (int e = 0; e < 4; ++e) cm[nt][e] += c1[nt][e] + (o0[nt][e] + o1[nt][e]);
 }
 
 // Stages the activations of every problem: each 8-element block (16 bytes)
 // is loaded from global memory, permuted to fragment order, and within each
 // 128-k chunk the sixteen blocks b = 4t + j (k = 32t + 8j) move to position
 // 4j + t, so a lane's LDS.128 for word j hits 16 consecutive bytes per t.  The
-// same pass forms the per-chunk sums sx[c][m] (fp32): a chunk's 16 blocks
+// same pass forms the per-chunk offsets sx[c][m] = -136 * sum x (fp32, the seed
+// of the chunk's MMA accumulator): a chunk's 16 blocks
 // belong to 16 consecutive lanes of one warp.  Work is handed out in units of
 // 32 blocks, one per lane, and every warp loads U units before it processes
 // any, so the loads of a warp are in flight together.  Plain loads rather than
@@ -346,7 +350,7 @@ __device__ __forceinline__ void stage_activations(const Params& P, uint8_t* xs, 
             *reinterpret_cast<uint4*>(row + pos * 16) =
                 make_uint4(prmt(v[b].x, v[b].z, 0x5410u), prmt(v[b].x, v[b].z, 0x7632u),
                            prmt(v[b].y, v[b].w, 0x5410u), prmt(v[b].y, v[b].w, 0x7632u));
-            if (r == 0) sx[(pr.sx_off + c) * kCols + ms[b]] = sum;
+            if (r == 0) sx[(pr.sx_off + c) * kCols + ms[b]] = -136.f * sum;
         }
     }
 }
@@ -379,7 +383,7 @@ __global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const
     const int group = warp / kGroupWarps, gw = warp % kGroupWarps;
     const int gtid = threadIdx.x % kGroupThreads;
     const int g = lane >> 2, t = lane & 3;
-    const int M = P.M, gshift = P.gshift, gs = P.gs, total = P.total_tiles;
+    const int M = P.M, gshift = P.gshift, total = P.total_tiles;
     const uint32_t magic = P.magic, neg136 = P.neg136;
     // group-major: consecutive tiles (the longest-K ones first) go to different
     // SMs before any SM gets a second one, which evens out the work per SM
@@ -432,14 +436,15 @@ __global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const
 
     const uint32_t ring_base = ring0 + g * 64 + 16 * t;
     uint32_t it = 0, ti = 0;
+    int pi = 0;
     for (int tile = first; tile < total; tile += stride, ++ti) {
-        const int pi = problem_index(P, tile);
+        while (pi + 1 < P.count && tile >= P.p[pi + 1].tile_begin) ++pi;
         const Prob& pr = P.p[pi];
         const int N = pr.N, K = pr.K, C = K >> 7;
         const int row0 = (tile - pr.tile_begin) * 16;
         const uint32_t sb = ti % kScaleBufs;
         sm100::mbar_wait(&S.sfull[group][sb], (ti / kScaleBufs) & 1u);
-        const int G = K / gs;
+        const int G = gshift == 31 ? 1 : (C >> gshift);  // K / gs without a division
         const uint32_t sa_base = sm100::smem_u32(&S.scales[group][sb][g * G]);
         const uint32_t sb_base = sa_base + 16 * G;  // row g + 8
         // activation rows of this lane's B fragments (columns >= M read row M - 1, discarded)
@@ -477,25 +482,28 @@ __global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const
                     load_x<NT, XS>(xrow, xsb, c, X);
                     const uint4 WA = lds128(st + j * kChunkBytes);
                     const uint4 WB = lds128(st + j * kChunkBytes + 512);
+                    // seeded with -136 * sum x of this chunk (columns 2t, 2t+1 of tile nt)
                     float cm[NT][4];
 #pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
+                    for (int nt = 0; nt < NT; ++nt) {
+                        if (XS) {
+                            const float2 o = lds_f2(sxp + (c * kCols + nt * 8) * 4);
+                            cm[nt][0] = o.x;
+                            cm[nt][1] = o.y;
+                            cm[nt][2] = o.x;
+                            cm[nt][3] = o.y;
+                        } else {
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) cm[nt][e] = 0.f;
+                            for (int e = 0; e < 4; ++e) cm[nt][e] = 0.f;
+                        }
+                    }
                     chunk_mma<NT, XS>(WA, WB, X, magic, neg136, cm);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
-                        // staged: minus 136 * sum x of this chunk (columns 2t, 2t+1 of tile nt)
-                        float c0 = 0.f, c1 = 0.f;
-                        if (XS) {
-                            const float2 sxv = lds_f2(sxp + (c * kCols + nt * 8) * 4);
-                            c0 = 136.f * sxv.x;
-                            c1 = 136.f * sxv.y;
-                        }
-                        acc[nt][0] = fmaf(sa, cm[nt][0] - c0, acc[nt][0]);
-                        acc[nt][1] = fmaf(sa, cm[nt][1] - c1, acc[nt][1]);
-                        acc[nt][2] = fmaf(sb2, cm[nt][2] - c0, acc[nt][2]);
-                        acc[nt][3] = fmaf(sb2, cm[nt][3] - c1, acc[nt][3]);
+                        acc[nt][0] = fmaf(sa, cm[nt][0], acc[nt][0]);
+                        acc[nt][1] = fmaf(sa, cm[nt][1], acc[nt][1]);
+                        acc[nt][2] = fmaf(sb2, cm[nt][2], acc[nt][2]);
+                        acc[nt][3] = fmaf(sb2, cm[nt][3], acc[nt][3]);
                     }
                 }
             }
@@ -656,7 +664,9 @@ int launch(Params& P, cudaStream_t stream) {
                                      CU_TENSOR_MAP_SWIZZLE_NONE);
         if (st != KC_OK) return st;
     }
-    // stage every problem's activations when they all fit
+    // stage every problem's activations when they all fit.  (Staging the chunk
+    // offsets alone when the activations do not fit was slower than the offset
+    // MMA: every CTA then reads all activations before its first tile.)
     const int NT = P.M <= 8 ? 1 : 2;
     long xs_bytes = 0, chunks = 0;  // padded footprint, chunk rows
     for (int i = 0; i < P.count; ++i) {

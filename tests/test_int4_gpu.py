@@ -203,6 +203,24 @@ def test_w4a16_grouped_matches_single(cuda):
         assert normwise_err(host(y), s) <= 1e-5
 
 
+@pytest.mark.parametrize("M,K,N", [(4, 11008, 96), (16, 12288, 24), (8, 36864, 16)])
+def test_w4a16_grouped_unstaged(cuda, M, K, N):
+    """Eight problems in one launch whose activations do not fit in shared
+    memory, so the kernel reads them from global memory and removes the offset
+    with the second MMA; every output is checked against the oracle."""
+    gs = 128
+    import kernel_craft_torch_ops as ops
+    probs, host_in = [], []
+    for i in range(8):
+        n = N + 16 * (i % 3)
+        packed, scales, x = _w4a16_inputs(M, n, K, gs, seed=300 + i)
+        host_in.append((packed, scales, x, n))
+        probs.append((dev(packed), dev(scales).view(torch.float16), _bf16_dev(x)))
+    outs = ops.w4a16_gemv_grouped(probs, gs)
+    for y, (packed, scales, x, n) in zip(outs, host_in):
+        assert normwise_err(host(y), O.gemv_w4a16(packed, scales, x, M, n, K, gs)) <= GEMV_TOL
+
+
 def test_w4a16_unaligned_takes_scalar_path(cuda):
     M, N, K, gs = 3, 40, 256, 128
     packed, scales, x = _w4a16_inputs(M, N, K, gs, seed=5)

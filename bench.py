@@ -1,7 +1,7 @@
 """bench.py -- benchmarks of the B200 quantized-linear library.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kc|reference]
-                    [--workload gemv|gemm_w4a16|gemm_fp8|quant_fp8|gemv_int4]
+                    [--workload gemv|gemm_w4a16|gemm_fp8|quant_fp8|gemv_int4|mlp_w4a16]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
 
 Default workload ("gemv", BASELINE config 2, the metric "W4A16 GEMV HBM
@@ -21,6 +21,9 @@ Other workloads (one line each, same keys):
   quant_fp8   config 1: per-token FP8 quantization of fp32 x [8192, 8192]
               with 1 % outlier channels (x20)
   gemv_int4   config 0: the reference ABI's fp32 INT4 GEMV, 4096 x 4096
+  mlp_w4a16   the reference's MLP block (col-parallel linear -> GELU ->
+              row-parallel linear -> all-reduce) on W4A16 weights, M=2048,
+              H=4096, I=16384, GELU in the first GEMM's epilogue, fp32 out
 
 At N > 1 every rank runs the same workload on its own GPU (replicas; a decode
 GEMV does not shard usefully at M = 1) and value is the aggregate.
@@ -666,7 +669,97 @@ class GemvInt4(Workload):
         return fn, b, "one config-0 GEMV per step"
 
 
-WORKLOADS = {w.name: w for w in (GemvW4A16, GemmW4A16, GemmFP8, QuantFP8, GemvInt4)}
+class MlpW4A16(Workload):
+    name = "mlp_w4a16"
+    metric = "W4A16 MLP block TFLOP/s (M=2048, H=4096, I=16384, GELU, group 128)"
+    unit = "TFLOP/s"
+    bound = "tensor-bf16"
+    dtype = "bf16"
+    data = "synthetic (seeded uniform INT4 nibbles, fp16 scales U[0.002,0.02], bf16 N(0,1))"
+    kernel = "gemm_w4a16"
+    profile = "gemm_w4a16_mlp_2048x4096x16384"
+    launches_per_step = 2
+    M, H, I = 2048, 4096, 16384
+    COPIES = 2
+
+    def __init__(self, torch, l, dev, s_ptr, rank, world=1):
+        super().__init__(torch, l, dev, s_ptr, rank, world)
+        import tp
+        M, H, I = self.M, self.H, self.I
+        self.i_shard = I // world           # W1 rows / W2 columns of this rank
+        xg = torch.Generator(device=dev)
+        xg.manual_seed(78)                  # activations are replicated: same on every rank
+        self.x = torch.randn(M, H, device=dev, generator=xg).bfloat16()
+        self.sets = []
+        for _ in range(self.COPIES):
+            w1p = torch.randint(0, 256, (self.i_shard, H // 2), dtype=torch.uint8, device=dev,
+                                generator=self.gen)
+            w1s = (torch.rand(self.i_shard, H // GROUP, device=dev, generator=self.gen) * 0.018
+                   + 0.002).half()
+            w2p = torch.randint(0, 256, (H, self.i_shard // 2), dtype=torch.uint8, device=dev,
+                                generator=self.gen)
+            w2s = (torch.rand(H, self.i_shard // GROUP, device=dev, generator=self.gen) * 0.018
+                   + 0.002).half()
+            self.sets.append((w1p, w1s, w2p, w2s))
+        self.blk = tp.MLPBlockW4A16(M, H, I, GROUP)
+        if world > 1:
+            self.scaling = "strong"
+        self.i = 0
+
+    def step(self):
+        self.blk(self.x, *self.sets[self.i % self.COPIES])
+        self.i += 1
+
+    def work_per_step(self):
+        return 4.0 * self.M * self.H * self.i_shard
+
+    def parallelism(self):
+        if self.world == 1:
+            return "single GPU"
+        return (f"tensor parallel x{self.world}: W1 rows and W2 columns I/{self.world} per GPU, "
+                "no communication between the GEMMs, one NCCL fp32 all-reduce per step")
+
+    def config(self):
+        return {"workload": "w4a16-mlp-block-2048x4096x16384", "M": self.M, "H": self.H,
+                "I": self.I, "group_size": GROUP, "activation": "gelu_quick (x*sigmoid(1.702x))",
+                "out": "fp32",
+                "l2": f"{self.COPIES} rotating weight sets of 66 MB each, and the 64 MB bf16 "
+                      "intermediate written and read per step (larger than L2 together)"}
+
+    def e2e_prepare(self):
+        self.h_x = self.x.cpu().pin_memory()
+        self.h_y = self.torch.empty(self.blk.y.shape, dtype=self.blk.y.dtype).pin_memory()
+        return self.h_x.numel() * 2, self.h_y.numel() * 4
+
+    def e2e_step(self):
+        self.x.copy_(self.h_x, non_blocking=True)
+        self.blk(self.x, *self.sets[0])
+        self.h_y.copy_(self.blk.y, non_blocking=True)
+
+    @classmethod
+    def _cpu(cls, rows):
+        O = _oracle()
+        w1p, w1s = O.make_w4_gptq(cls.I, cls.H, GROUP, seed=40)
+        w2p, w2s = O.make_w4_gptq(cls.H, cls.I, GROUP, seed=41)
+        x = O.make_activations_bf16(rows, cls.H, seed=42)
+        return (lambda: O.mlp_block_w4a16(x, w1p, w1s, w2p, w2s, rows, cls.H, cls.I, GROUP)), \
+            4.0 * rows * cls.H * cls.I
+
+    @classmethod
+    def cpu_sample(cls):
+        fn, flops = cls._cpu(8)
+        dt, reps = _timed_sample(fn, max_reps=20)
+        return {"value": round(flops / dt / 1e12, 5), "unit": "TFLOP/s",
+                "cores": os.cpu_count() or 1, "kind": "port",
+                "sample": f"8 of 2048 token rows through the whole block, {reps} reps"}
+
+    @classmethod
+    def reference_step(cls):
+        fn, flops = cls._cpu(8)
+        return fn, flops, "8 of 2048 token rows through the whole block per step"
+
+
+WORKLOADS = {w.name: w for w in (GemvW4A16, GemmW4A16, GemmFP8, QuantFP8, GemvInt4, MlpW4A16)}
 
 
 # --------------------------------------------------------------------------

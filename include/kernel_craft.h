@@ -258,6 +258,22 @@ KC_API int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const ui
                          void* out, int out_f32, int M, int N, int K, int group_size, int ldc,
                          cudaStream_t stream);
 
+/* Activations the W4A16 GEMM epilogue can apply to the fp32 accumulator. */
+#define KC_ACT_NONE       0
+#define KC_ACT_GELU_QUICK 1   /* x * sigmoid(1.702 x): the reference MLP block's GELU,
+                                 examples/python/transformer/tensor_parallel.py:162 */
+
+/* kc_gemm_w4a16 with an activation applied in the epilogue, before the
+ * rounding to bf16 (or the fp32 store): the first linear of the reference's
+ * column-parallel -> GELU -> row-parallel MLP block
+ * (examples/python/transformer/tensor_parallel.py:150-172), where
+ * launch_col_parallel_linear (tensor_parallel.cu:209) and a separate numpy
+ * GELU run in two passes.  Same arguments and requirements as kc_gemm_w4a16;
+ * act is KC_ACT_NONE or KC_ACT_GELU_QUICK. */
+KC_API int kc_gemm_w4a16_act(const uint16_t* x_bf16, const uint8_t* packed,
+                             const uint16_t* scales_f16, void* out, int out_f32, int M, int N,
+                             int K, int group_size, int ldc, int act, cudaStream_t stream);
+
 /* Column-parallel W4A16 GEMM fused with the all-gather of its output (one
  * process per GPU; no counterpart kernel in the reference, whose
  * launch_col_parallel_linear + launch_allgather_nccl, tensor_parallel.cu:209 and

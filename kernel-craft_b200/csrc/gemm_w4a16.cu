@@ -24,7 +24,9 @@
 //    the MMA as soon as the last load returns, convert to bf16 into a
 //    shared-memory tile and write it with a TMA store that runs under the next
 //    tile's main loop (fp32 output, or a pitch the TMA cannot address, falls
-//    back to direct coalesced stores).
+//    back to direct coalesced stores).  An optional activation (the
+//    sigmoid-approximated GELU of the reference's MLP block) is applied to the
+//    fp32 accumulator before the conversion.
 // TMEM holds one accumulator only (256 + 128 A columns of 512), so the early
 // release keeps the MMA idle per tile to the drain time.  Staging bf16 weights
 // in shared memory instead would need ~160 B/clk of shared-memory bandwidth per
@@ -60,12 +62,21 @@ struct alignas(64) Params {
     const __half* scales;
     void* out;
     int M, N, K, gs, ldc, out_f32, tma_out;
+    int act;       // KC_ACT_NONE or KC_ACT_GELU_QUICK, applied in the epilogue
     int ndst;      // destination buffers of each tile (1, or the ranks of an all-gather)
     int col_off;   // first output column of this launch's N rows in every destination
     int tiles_w, tiles_t;
     uint32_t magic;     // 0x3F800000 (1.0f), kept in a register
     uint32_t gs_recip;      // ceil(2^32 / gs): k / gs == umulhi(k, gs_recip) for k * gs < 2^32
 };
+
+// The reference MLP block's activation, x * sigmoid(1.702 x)
+// (examples/python/transformer/tensor_parallel.py:162), in fp32: __expf of a
+// large positive argument gives inf and the quotient -0, of a large negative
+// one 0 and the quotient x.
+__device__ __forceinline__ float activate(float v, int act) {
+    return act == KC_ACT_GELU_QUICK ? __fdividef(v, 1.f + __expf(-1.702f * v)) : v;
+}
 
 struct Smem {
     uint8_t x[kStages][kXBytes];   // 1024-byte aligned (swizzle atoms)
@@ -287,8 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
                     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + c * 64 * BW + q * 32 + lane;
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        o[i * BW] = __float2bfloat16_rn(__uint_as_float(r[i]));
-                        o[(32 + i) * BW] = __float2bfloat16_rn(__uint_as_float(r2[i]));
+                        o[i * BW] = __float2bfloat16_rn(activate(__uint_as_float(r[i]), P.act));
+                        o[(32 + i) * BW] = __float2bfloat16_rn(activate(__uint_as_float(r2[i]), P.act));
                     }
                 }
                 sm100::fence_proxy_async_smem();
@@ -312,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             if (mb + i < P.M) {
-                                const float f = __uint_as_float(r[i]);
+                                const float f = activate(__uint_as_float(r[i]), P.act);
                                 if (P.out_f32)
                                     reinterpret_cast<float*>(P.out)[(size_t)(mb + i) * P.ldc + n] = f;
                                 else
@@ -347,9 +358,11 @@ namespace {
 // single destination, fp32 / unaligned output through direct stores.
 int launch_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
                       void* const* outs, int ndst, int col_off, int out_cols, int out_f32, int M,
-                      int N, int K, int group_size, int ldc, cudaStream_t stream) {
+                      int N, int K, int group_size, int ldc, int act, cudaStream_t stream) {
     KC_REQUIRE(x_bf16 && packed && scales_f16 && outs && outs[0], KC_ERR_INVALID_ARG,
                "null pointer argument");
+    KC_REQUIRE(act == KC_ACT_NONE || act == KC_ACT_GELU_QUICK, KC_ERR_INVALID_ARG,
+               "unknown activation %d", act);
     KC_REQUIRE(M >= 0 && N >= 0 && K >= 0, KC_ERR_INVALID_ARG, "negative size");
     if (M == 0 || N == 0) return KC_OK;
     KC_REQUIRE(K > 0 && K % BK == 0, KC_ERR_INVALID_ARG, "K=%d must be a positive multiple of %d", K, BK);
@@ -391,6 +404,7 @@ int launch_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint1
     P.gs = group_size;
     P.ldc = ldc;
     P.out_f32 = out_f32 ? 1 : 0;
+    P.act = act;
     P.tiles_w = (N + BW - 1) / BW;
     P.tiles_t = (M + BT - 1) / BT;
     P.magic = 0x3F800000u;
@@ -413,7 +427,15 @@ int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t*
                   cudaStream_t stream) {
     void* outs[1] = {out};
     return launch_gemm_w4a16(x_bf16, packed, scales_f16, outs, 1, 0, N, out_f32, M, N, K,
-                             group_size, ldc, stream);
+                             group_size, ldc, KC_ACT_NONE, stream);
+}
+
+int kc_gemm_w4a16_act(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
+                      void* out, int out_f32, int M, int N, int K, int group_size, int ldc, int act,
+                      cudaStream_t stream) {
+    void* outs[1] = {out};
+    return launch_gemm_w4a16(x_bf16, packed, scales_f16, outs, 1, 0, N, out_f32, M, N, K,
+                             group_size, ldc, act, stream);
 }
 
 int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed_shard,
@@ -428,7 +450,7 @@ int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed_shard,
     const long cols = (long)N_shard * nranks;
     KC_REQUIRE(cols < (1L << 31), KC_ERR_INVALID_ARG, "output too wide");
     return launch_gemm_w4a16(x_bf16, packed_shard, scales_shard, outs, nranks, rank * N_shard,
-                             (int)cols, 0, M, N_shard, K, group_size, (int)cols, stream);
+                             (int)cols, 0, M, N_shard, K, group_size, (int)cols, KC_ACT_NONE, stream);
 }
 
 }  // extern "C"

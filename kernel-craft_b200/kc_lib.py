@@ -31,6 +31,8 @@ KC_ERR_UNSUPPORTED = 5
 KC_ERR_TIMEOUT = 6
 KC_W4A16_MAX_PROBLEMS = 8
 KC_MAX_RANKS = 8
+KC_ACT_NONE = 0
+KC_ACT_GELU_QUICK = 1
 
 
 class KcError(RuntimeError):
@@ -90,6 +92,7 @@ _PROTOS = [
     ("kc_sgemm_nt", ci, [vp, vp, vp, ci, ci, ci, vp]),
     ("kc_gemm_fp8", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, vp]),
+    ("kc_gemm_w4a16_act", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16_allgather", ci, [vp, vp, vp, ctypes.POINTER(vp), ci, ci, ci, ci, ci, ci, vp]),
     ("kc_allreduce_bf16_peer", ci, [ctypes.POINTER(vp), ctypes.POINTER(vp), ci, ci, cl, vp]),
     ("kc_peer_barrier", ci, [ctypes.POINTER(vp), ci, ci, ci, vp]),

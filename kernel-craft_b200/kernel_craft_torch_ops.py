@@ -200,10 +200,18 @@ def w4a16_gemv_grouped(problems: Sequence[Tuple[torch.Tensor, torch.Tensor, torc
     return outs
 
 
-def w4a16_gemm(x, packed, scales_f16, group_size: int = 128, out_dtype=torch.bfloat16):
-    """C[M, N] = x[M, K] (bf16) . W^T on the tcgen05 tensor cores, W the GPTQ W4
-    [N, K] (packed u8 [N, K/2], fp16 scales [N, K/gs]); fp32 accumulation,
-    bf16 (default) or fp32 output."""
+_ACTIVATIONS = {"none": kc_lib.KC_ACT_NONE, "gelu_quick": kc_lib.KC_ACT_GELU_QUICK}
+
+
+def w4a16_gemm(x, packed, scales_f16, group_size: int = 128, out_dtype=torch.bfloat16,
+               activation: str = "none"):
+    """C[M, N] = act(x[M, K] (bf16) . W^T) on the tcgen05 tensor cores, W the
+    GPTQ W4 [N, K] (packed u8 [N, K/2], fp16 scales [N, K/gs]); fp32
+    accumulation, bf16 (default) or fp32 output.  activation "gelu_quick"
+    applies x * sigmoid(1.702 x), the reference MLP block's GELU
+    (examples/python/transformer/tensor_parallel.py:162), in the epilogue."""
+    if activation not in _ACTIVATIONS:
+        raise ValueError(f"activation must be one of {sorted(_ACTIVATIONS)}")
     x, packed, scales_f16 = x.contiguous(), packed.contiguous(), scales_f16.contiguous()
     _require_cuda(x, packed, scales_f16)
     m, k = x.shape
@@ -212,9 +220,9 @@ def w4a16_gemm(x, packed, scales_f16, group_size: int = 128, out_dtype=torch.bfl
         raise ValueError(f"x has K={k}, packed weights K={packed.shape[1] * 2}")
     out = torch.empty(m, n, dtype=out_dtype, device=x.device)
     with kernel_span("w4a16_gemm", rows=n, cols=k, batch=m, group_size=group_size):
-        check(lib().kc_gemm_w4a16(_ptr(x), _ptr(packed), _ptr(scales_f16), _ptr(out),
-                                  1 if out_dtype == torch.float32 else 0, m, n, k, group_size, n,
-                                  _stream()))
+        check(lib().kc_gemm_w4a16_act(_ptr(x), _ptr(packed), _ptr(scales_f16), _ptr(out),
+                                      1 if out_dtype == torch.float32 else 0, m, n, k, group_size,
+                                      n, _ACTIVATIONS[activation], _stream()))
     return out
 
 

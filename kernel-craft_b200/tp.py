@@ -21,6 +21,12 @@ tensor_parallel_nccl.cu:105-135):
   slice from all partials and writes it to every rank); ``row_parallel_fp8``
   is the same linear with an NCCL all-reduce instead.
 
+* the MLP block (the reference's col-parallel -> GELU -> row-parallel chain,
+  examples/python/transformer/tensor_parallel.py:150-172): ``MLPBlockW4A16``
+  runs the up projection on its rows of W1 with the GELU in the GEMM epilogue
+  (``kc_gemm_w4a16_act``), the down projection on the same columns of W2 into
+  an fp32 partial, and one all-reduce; no communication between the two GEMMs.
+
 The process group must be NCCL for the GPU collectives; every rank calls the
 same functions in the same order.
 """
@@ -264,3 +270,72 @@ def row_parallel_fp8(a_codes_shard: torch.Tensor, sa: torch.Tensor, w_codes_shar
                             ctypes.c_void_p(out.data_ptr()), 0, M, N, Kr, out.stride(0), _stream()))
     dist.all_reduce(out, group=comm_group)
     return out
+
+
+def shard_w4_rows(packed: torch.Tensor, scales: torch.Tensor, world: int, rank: int):
+    """Rows [r*N/R, (r+1)*N/R) of a W4 matrix [N, K] (packed u8 [N, K/2],
+    scales [N, K/gs]): the weight shard of a column-parallel linear."""
+    b, e = shard_range(packed.shape[0], world, rank)
+    return packed[b:e].contiguous(), scales[b:e].contiguous()
+
+
+def shard_w4_cols(packed: torch.Tensor, scales: torch.Tensor, group_size: int, world: int, rank: int):
+    """Columns [r*K/R, (r+1)*K/R) of a W4 matrix [N, K]: the weight shard of a
+    row-parallel linear.  K/R must be a multiple of the group size, so each
+    shard keeps whole scale groups (packed bytes hold two k each)."""
+    K = packed.shape[1] * 2
+    b, e = shard_range(K, world, rank)
+    if (e - b) % group_size:
+        raise ValueError(f"K shard {e - b} is not a multiple of the group size {group_size}")
+    return (packed[:, b // 2:e // 2].contiguous(),
+            scales[:, b // group_size:e // group_size].contiguous())
+
+
+class MLPBlockW4A16:
+    """The reference's MLP block on GPTQ W4 weights, tensor parallel.
+
+    x [M, H] bf16 is replicated.  Rank r holds rows [r*I/R, (r+1)*I/R) of the
+    up projection W1 [I, H] (``shard_w4_rows``) and the same columns of the
+    down projection W2 [H, I] (``shard_w4_cols``).  ``__call__`` computes
+    h_r = gelu_quick(x . W1_r^T) with the activation in the GEMM epilogue
+    (bf16, [M, I/R]), the partial y_r = h_r . W2_r^T in fp32, and sums the
+    partials with one NCCL all-reduce; every rank returns y [M, H] fp32.  The
+    reference's block runs the same chain (tensor_parallel.py:150-172:
+    col_parallel_linear, a numpy GELU, row_parallel_linear, ring_allreduce) in
+    fp32 with the activation as a separate pass.  With one process (or no
+    process group) it is the plain two-GEMM block."""
+
+    def __init__(self, M: int, H: int, I: int, group_size: int = 128, act: str = "gelu_quick",
+                 group=None):
+        if act not in ("gelu_quick", "none"):
+            raise ValueError("act must be 'gelu_quick' or 'none'")
+        self.act = kc_lib.KC_ACT_GELU_QUICK if act == "gelu_quick" else kc_lib.KC_ACT_NONE
+        self.group = group
+        dist_on = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if dist_on else 1
+        self.rank = dist.get_rank(group) if dist_on else 0
+        self.M, self.H, self.I, self.gs = M, H, I, group_size
+        b, e = shard_range(I, self.world, self.rank)
+        self.i_shard = e - b
+        if self.i_shard % group_size or self.i_shard % 64:
+            raise ValueError(f"I/R = {self.i_shard} must be a multiple of 64 and of the group size")
+        self.h = torch.empty(M, self.i_shard, dtype=torch.bfloat16, device="cuda")
+        self.y = torch.empty(M, H, dtype=torch.float32, device="cuda")
+
+    def launch(self, x, w1_packed, w1_scales, w2_packed, w2_scales) -> None:
+        """Both GEMMs of this rank (no collective): for timing."""
+        l = lib()
+        check(l.kc_gemm_w4a16_act(
+            ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w1_packed.data_ptr()),
+            ctypes.c_void_p(w1_scales.data_ptr()), ctypes.c_void_p(self.h.data_ptr()), 0, self.M,
+            self.i_shard, self.H, self.gs, self.i_shard, self.act, _stream()))
+        check(l.kc_gemm_w4a16(
+            ctypes.c_void_p(self.h.data_ptr()), ctypes.c_void_p(w2_packed.data_ptr()),
+            ctypes.c_void_p(w2_scales.data_ptr()), ctypes.c_void_p(self.y.data_ptr()), 1, self.M,
+            self.H, self.i_shard, self.gs, self.H, _stream()))
+
+    def __call__(self, x, w1_packed, w1_scales, w2_packed, w2_scales) -> torch.Tensor:
+        self.launch(x, w1_packed, w1_scales, w2_packed, w2_scales)
+        if self.world > 1:
+            dist.all_reduce(self.y, group=self.group)
+        return self.y

@@ -118,6 +118,30 @@ def gemm_w4a16(a_bf16_bits, packed, scales_f16, M, N, K, gs) -> np.ndarray:
     return c
 
 
+def gelu_quick(h) -> np.ndarray:
+    """x * sigmoid(1.702 x) in fp32, the activation of the reference's MLP block
+    (examples/python/transformer/tensor_parallel.py:162)."""
+    h = np.asarray(h, np.float32)
+    with np.errstate(over="ignore"):
+        return (h * (np.float32(1) / (np.float32(1) + np.exp(np.float32(-1.702) * h)))).astype(np.float32)
+
+
+def mlp_block_w4a16(x_bf16_bits, w1_packed, w1_scales_f16, w2_packed, w2_scales_f16, M, H, I, gs,
+                    act: str = "gelu_quick") -> np.ndarray:
+    """The reference's MLP block (col-parallel linear -> GELU -> row-parallel
+    linear -> all-reduce, examples/python/transformer/tensor_parallel.py:150-172;
+    without the activation, test_tensor_parallel.cpp:339-376) on W4A16 weights:
+    h = act(x . W1^T) in fp32 (W1 [I, H]), rounded to bf16 as the input of the
+    second GEMM, y = h . W2^T in fp32 (W2 [H, I]).  A sharded run computes the
+    same y as the sum over ranks of h[:, shard] . W2[:, shard]^T."""
+    h = gemm_w4a16(x_bf16_bits, w1_packed, w1_scales_f16, M, I, H, gs)
+    if act == "gelu_quick":
+        h = gelu_quick(h)
+    elif act != "none":
+        raise ValueError(act)
+    return gemm_w4a16(f32_to_bf16_bits(h), w2_packed, w2_scales_f16, M, H, I, gs)
+
+
 # --------------------------------------------------------------------------
 # FP8
 # --------------------------------------------------------------------------

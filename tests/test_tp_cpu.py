@@ -4,7 +4,11 @@ the gathered / reduced results must equal the unsharded oracle (column
 parallel bit for bit: every output column is computed by exactly one rank with
 the same arithmetic; row parallel within fp32 summation-order noise: the
 reference's launch_row_parallel_linear + all-reduce, tensor_parallel.cu:235,
-adds the rank partials in another order than one full-K sum)."""
+adds the rank partials in another order than one full-K sum).  The MLP block
+(the reference's col-parallel -> GELU -> row-parallel chain,
+examples/python/transformer/tensor_parallel.py:150-172) is sharded the way
+tp.MLPBlockW4A16 shards it: W1 by rows, W2 by the same columns, one
+all-reduce."""
 import os
 import socket
 
@@ -15,7 +19,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle as O
-from tp import shard_range
+from tp import shard_range, shard_w4_cols, shard_w4_rows
 
 M, N, K, GS = 24, 256, 512, 128
 
@@ -77,3 +81,54 @@ def test_shard_range():
         shard_range(100, 3, 0)
     with pytest.raises(ValueError):
         shard_range(100, 2, 2)
+
+
+MH, MI = 256, 512      # MLP block: hidden H, intermediate I
+
+
+def _mlp_inputs():
+    w1p, w1s = O.make_w4_gptq(MI, MH, GS, seed=21)     # W1 [I, H]
+    w2p, w2s = O.make_w4_gptq(MH, MI, GS, seed=22)     # W2 [H, I]
+    x = O.make_activations_bf16(M, MH, seed=23)
+    return w1p, w1s, w2p, w2s, x
+
+
+def _mlp_rank_main(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w1p, w1s, w2p, w2s, x = _mlp_inputs()
+        p1, s1 = shard_w4_rows(torch.from_numpy(w1p), torch.from_numpy(w1s.view(np.uint16)), world, rank)
+        p2, s2 = shard_w4_cols(torch.from_numpy(w2p), torch.from_numpy(w2s.view(np.uint16)), GS, world,
+                               rank)
+        ir = MI // world
+        h = O.gelu_quick(O.gemm_w4a16(x, p1.numpy(), s1.numpy().view(np.float16), M, ir, MH, GS))
+        part = torch.from_numpy(O.gemm_w4a16(O.f32_to_bf16_bits(h), p2.numpy(),
+                                             s2.numpy().view(np.float16), M, MH, ir, GS))
+        dist.all_reduce(part)
+        if rank == 0:
+            np.save(os.path.join(out_dir, "mlp.npy"), part.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_mlp_block_matches_unsharded(tmp_path):
+    world = 2
+    mp.spawn(_mlp_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    w1p, w1s, w2p, w2s, x = _mlp_inputs()
+    full = O.mlp_block_w4a16(x, w1p, w1s, w2p, w2s, M, MH, MI, GS)
+    got = np.load(tmp_path / "mlp.npy")
+    assert np.max(np.abs(got - full)) / np.max(np.abs(full)) <= 1e-6
+
+
+def test_w4_shard_helpers():
+    packed = torch.arange(8 * 128, dtype=torch.int32).reshape(8, 128).to(torch.uint8)
+    scales = torch.arange(8 * 4, dtype=torch.int16).reshape(8, 4)     # K = 256, gs = 64
+    p, s = shard_w4_rows(packed, scales, 2, 1)
+    assert torch.equal(p, packed[4:]) and torch.equal(s, scales[4:])
+    p, s = shard_w4_cols(packed, scales, 64, 2, 1)
+    assert torch.equal(p, packed[:, 64:]) and torch.equal(s, scales[:, 2:])
+    assert p.is_contiguous() and s.is_contiguous()
+    assert shard_w4_cols(packed, scales, 64, 4, 3)[1].shape == (8, 1)   # K shard 64: one group
+    with pytest.raises(ValueError):
+        shard_w4_cols(packed, scales, 64, 8, 0)      # K shard 32 would split a scale group

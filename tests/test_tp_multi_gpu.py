@@ -7,7 +7,10 @@ stored, unchanged, into every rank's buffer).  Row parallel: the K-sharded FP8
 GEMM + bf16 sum -- by NCCL all-reduce and by the peer-memory kernel
 kc_allreduce_bf16_peer -- against the single-GPU FP8 GEMM, normwise <= 1e-2
 (bf16 partials are rounded before the sum); the peer sum is identical on
-every rank.  Skipped with fewer than 2 GPUs.
+every rank.  MLP block (tp.MLPBlockW4A16, the reference's col-parallel ->
+GELU -> row-parallel chain): the sharded block against the two unsharded
+GEMMs on one GPU, normwise <= 1e-5 (the activations are the same bits; only
+the fp32 order of the K sum differs).  Skipped with fewer than 2 GPUs.
 """
 import datetime
 import os
@@ -80,9 +83,29 @@ def _rank_main(rank, world, port, out_dir):
         dist.all_gather(gathered, y2.clone())
         row_same = all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16)) for g in gathered)
         rp.close()
+
+        # MLP block: W1 [I, H] by rows, W2 [H, I] by the same columns, one all-reduce
+        M3, H3, I3 = 200, 512, 2048
+        x3 = torch.randn(M3, H3, device="cuda", generator=g).bfloat16()
+        w1p = torch.randint(0, 256, (I3, H3 // 2), dtype=torch.uint8, device="cuda", generator=g)
+        w1s = (torch.rand(I3, H3 // gs, device="cuda", generator=g) * 0.018 + 0.002).half()
+        w2p = torch.randint(0, 256, (H3, I3 // 2), dtype=torch.uint8, device="cuda", generator=g)
+        w2s = (torch.rand(H3, I3 // gs, device="cuda", generator=g) * 0.018 + 0.002).half()
+        h_full = torch.empty(M3, I3, dtype=torch.bfloat16, device="cuda")
+        y_full = torch.empty(M3, H3, dtype=torch.float32, device="cuda")
+        kc_lib.check(l.kc_gemm_w4a16_act(x3.data_ptr(), w1p.data_ptr(), w1s.data_ptr(), h_full.data_ptr(),
+                                         0, M3, I3, H3, gs, I3, kc_lib.KC_ACT_GELU_QUICK, st))
+        kc_lib.check(l.kc_gemm_w4a16(h_full.data_ptr(), w2p.data_ptr(), w2s.data_ptr(), y_full.data_ptr(),
+                                     1, M3, H3, I3, gs, H3, st))
+        p1, s1 = tp.shard_w4_rows(w1p, w1s, world, rank)
+        p2, s2 = tp.shard_w4_cols(w2p, w2s, gs, world, rank)
+        mlp = tp.MLPBlockW4A16(M3, H3, I3, gs)
+        y3 = mlp(x3, p1, s1, p2, s2)
+        torch.cuda.synchronize()
+        mlp_err = float((y3 - y_full).abs().max() / y_full.abs().max())
         status = l.kc_get_device_status()
         np.save(os.path.join(out_dir, f"rank{rank}.npy"),
-                np.array([col_ok, row_err, status, row_same], dtype=np.float64))
+                np.array([col_ok, row_err, status, row_same, mlp_err], dtype=np.float64))
         col.close()
     finally:
         dist.destroy_process_group()
@@ -94,8 +117,9 @@ def test_tensor_parallel_two_gpus(tmp_path):
     import torch.multiprocessing as mp
     mp.spawn(_rank_main, args=(WORLD, _free_port(), str(tmp_path)), nprocs=WORLD, join=True)
     for r in range(WORLD):
-        col_ok, row_err, status, row_same = np.load(tmp_path / f"rank{r}.npy")
+        col_ok, row_err, status, row_same, mlp_err = np.load(tmp_path / f"rank{r}.npy")
         assert row_same == 1.0, "peer all-reduce outputs differ between ranks"
         assert col_ok == 1.0, f"rank {r}: gathered W4A16 output differs from the single-GPU GEMM"
         assert row_err <= 1e-2, f"rank {r}: row-parallel FP8 error {row_err}"
+        assert mlp_err <= 1e-5, f"rank {r}: MLP block error {mlp_err}"
         assert status == 0

@@ -102,6 +102,12 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
+            # nvidia-smi can take seconds to print its first sample (longer
+            # while other ranks start theirs): wait for it, so the heat phase
+            # and the timed region that follow are sampled
+            t0 = time.perf_counter()
+            while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 10.0:
+                time.sleep(0.05)
         except (FileNotFoundError, OSError):
             self.proc = None
 

@@ -1,0 +1,149 @@
+"""checkpoint -- GPTQ / AWQ checkpoint tensors -> this library's INT4 weight layouts.
+
+Host-side (numpy), run once when weights are loaded.  The reference has no
+loader: its kernels take a W4 matrix W [N, K] (N output channels) as packed
+bytes [N, K/2] with the low nibble holding the even k (quant_int4.cu:34-48),
+and this library's W4A16 GEMV / GEMM read that layout with fp16 scales
+[N, K/gs] and the implicit zero point 8 (w = (u - 8) * s).  Checkpoints store
+the same integers in other layouts:
+
+* GPTQ (AutoGPTQ "gptq" and "gptq_v2" formats): qweight int32 [K/8, N], input
+  channel k = 8*i + j in bits 4j..4j+3 of qweight[i, n]; qzeros int32
+  [K/gs, N/8], output channel n = 8*c + j in bits 4j.. of qzeros[g, c], stored
+  as z - 1 in the "gptq" format and as z in "gptq_v2"; scales fp16 [K/gs, N];
+  g_idx int32 [K] the group of input channel k (act order, "desc_act",
+  assigns groups out of k order).
+* AWQ: qweight int32 [K, N/8] and qzeros int32 [K/gs, N/8], output channel
+  n = 8*c + j in bits 4*p.. with p = (0, 4, 1, 5, 2, 6, 3, 7)[j] (the packing
+  interleave (0, 2, 4, 6, 1, 3, 5, 7)); scales fp16 [K/gs, N];
+  w = (q - z) * s.
+
+These are the layouts vLLM 0.22.0 packs and unpacks
+(vllm/model_executor/layers/quantization/utils/quant_utils.py: pack_rows,
+pack_cols, awq_pack; awq_triton.py's reverse order), which the tests use as
+the independent packer.
+
+The W4A16 kernels compute (u - 8) * s, so only symmetric checkpoints (every
+zero point 8) convert; others raise ValueError.  Act-order checkpoints convert
+with a permutation of the input channels that makes every group contiguous:
+the kernels then take x[:, perm] instead of x (a gather, or folded into the
+producer of x).
+"""
+from __future__ import annotations
+
+from typing import NamedTuple, Optional, Tuple
+
+import numpy as np
+
+_AWQ_SHIFT_OF_COL = np.array([0, 4, 1, 5, 2, 6, 3, 7])   # nibble position of column j of a word
+
+
+class W4A16Weights(NamedTuple):
+    packed: np.ndarray             # u8 [N, K/2], low nibble = even k
+    scales: np.ndarray             # fp16 [N, K/gs]
+    perm: Optional[np.ndarray]     # int64 [K]: the kernels take x[:, perm]; None = identity
+
+
+def _np(a) -> np.ndarray:
+    """numpy view of an array or a (CPU or CUDA) torch tensor."""
+    if hasattr(a, "detach"):
+        a = a.detach().cpu().numpy()
+    return np.asarray(a)
+
+
+def _nibbles_rows(q: np.ndarray) -> np.ndarray:
+    """int32 [R, C] holding 8 nibbles per word along the rows -> u8 [8R, C]."""
+    w = q.astype(np.uint32)
+    out = np.empty((w.shape[0] * 8, w.shape[1]), np.uint8)
+    for j in range(8):
+        out[j::8] = (w >> (4 * j)) & 0xF
+    return out
+
+
+def _nibbles_cols(q: np.ndarray, shift_of_col=None) -> np.ndarray:
+    """int32 [R, C] holding 8 nibbles per word along the columns -> u8 [R, 8C];
+    column 8c + j sits at nibble position shift_of_col[j] (default j)."""
+    w = q.astype(np.uint32)
+    out = np.empty((w.shape[0], w.shape[1] * 8), np.uint8)
+    for j in range(8):
+        p = j if shift_of_col is None else int(shift_of_col[j])
+        out[:, j::8] = (w >> (4 * p)) & 0xF
+    return out
+
+
+def _pack_w4(u_kn: np.ndarray) -> np.ndarray:
+    """u8 [K, N] integers 0..15 -> the library's packed u8 [N, K/2]."""
+    u = u_kn.T
+    return np.ascontiguousarray(u[:, 0::2] | (u[:, 1::2] << 4)).astype(np.uint8)
+
+
+def _check_symmetric(z: np.ndarray, what: str) -> None:
+    if not np.all(z == 8):
+        bad = int(np.count_nonzero(z != 8))
+        raise ValueError(f"{what}: {bad} zero points differ from 8; the W4A16 kernels compute "
+                         "(u - 8) * s and take symmetric checkpoints only")
+
+
+def _group_order(g_idx: np.ndarray, K: int, group_size: int) -> Optional[np.ndarray]:
+    """None when g_idx is the plain k // group_size, else the stable order of
+    the input channels by group (each group then holds group_size consecutive
+    channels)."""
+    g = _np(g_idx).astype(np.int64).reshape(-1)
+    if g.shape[0] != K:
+        raise ValueError(f"g_idx has {g.shape[0]} entries for K = {K}")
+    if np.array_equal(g, np.arange(K) // group_size):
+        return None
+    counts = np.bincount(g, minlength=K // group_size)
+    if counts.shape[0] != K // group_size or np.any(counts != group_size):
+        raise ValueError("g_idx must assign exactly group_size input channels to every group")
+    return np.argsort(g, kind="stable")
+
+
+def from_gptq(qweight, qzeros, scales, g_idx=None, group_size: int = 128,
+              checkpoint_format: str = "gptq") -> W4A16Weights:
+    """GPTQ tensors (qweight int32 [K/8, N], qzeros int32 [K/gs, N/8], scales
+    fp16 [K/gs, N], optional g_idx [K]) -> the W4A16 layout.
+    checkpoint_format "gptq" stores zero points minus one, "gptq_v2" as is."""
+    if checkpoint_format not in ("gptq", "gptq_v2"):
+        raise ValueError("checkpoint_format must be 'gptq' or 'gptq_v2'")
+    qw, qz, s = _np(qweight), _np(qzeros), _np(scales)
+    u = _nibbles_rows(qw)                                  # [K, N]
+    K, N = u.shape
+    if K % group_size or s.shape != (K // group_size, N):
+        raise ValueError(f"scales {s.shape} do not match K={K}, N={N}, group_size={group_size}")
+    z = _nibbles_cols(qz)[:, :N].astype(np.int32)          # [K/gs, N]
+    if checkpoint_format == "gptq":
+        z = (z + 1) & 0xF
+    _check_symmetric(z, "GPTQ checkpoint")
+    perm = None if g_idx is None else _group_order(g_idx, K, group_size)
+    if perm is not None:
+        u = u[perm]
+    return W4A16Weights(_pack_w4(u), np.ascontiguousarray(s.T).astype(np.float16), perm)
+
+
+def from_awq(qweight, qzeros, scales, group_size: int = 128) -> W4A16Weights:
+    """AWQ tensors (qweight int32 [K, N/8], qzeros int32 [K/gs, N/8], scales
+    fp16 [K/gs, N]) -> the W4A16 layout."""
+    qw, qz, s = _np(qweight), _np(qzeros), _np(scales)
+    u = _nibbles_cols(qw, _AWQ_SHIFT_OF_COL)               # [K, N]
+    K, N = u.shape
+    if K % group_size or s.shape != (K // group_size, N):
+        raise ValueError(f"scales {s.shape} do not match K={K}, N={N}, group_size={group_size}")
+    z = _nibbles_cols(qz, _AWQ_SHIFT_OF_COL)[:, :N]
+    _check_symmetric(z, "AWQ checkpoint")
+    return W4A16Weights(_pack_w4(u), np.ascontiguousarray(s.T).astype(np.float16), None)
+
+
+def to_reference_abi(w: W4A16Weights, group_size: int = 128) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """The same weights for the reference ABI (launch_dequantize_int4 /
+    launch_gemv_int4, quant_int4.cu:68-105): weight nibbles as sign-extended
+    two's complement (sx4(u ^ 8) = u - 8, so packed ^ 0x88), fp32 scales
+    [N, K/gs], and zero points 0 in the row stride the reference kernel reads,
+    floor(K/gs/2) bytes (quant_int4.cu:93; its tests allocate the ceiling,
+    test_quant_int4.cpp:56, which only differs for an odd group count, where
+    all-zero points read the same either way).  One trailing byte keeps the
+    last row's odd group inside the buffer."""
+    packed = np.ascontiguousarray(w.packed ^ np.uint8(0x88))
+    N, G = w.scales.shape
+    zeros = np.zeros(N * (G // 2) + 1, np.uint8)
+    return packed, w.scales.astype(np.float32), zeros

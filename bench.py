@@ -228,6 +228,14 @@ class GemvW4A16(Workload):
         self.n_layers = layers
         self.launches_per_step = layers
         self.layers = []
+        # every activation and every output of a step in one buffer each, so
+        # the end-to-end step moves them with one copy in and one copy out
+        # (each problem's slice stays 16-byte aligned: K*2 and N*4 bytes)
+        kx = sum(K for _, K, _ in SHAPES)
+        ny = sum(N for _, _, N in SHAPES)
+        self.x_all = torch.randn(layers * kx, device=dev, generator=self.gen).bfloat16()
+        self.y_all = torch.empty(layers * ny, dtype=torch.float32, device=dev)
+        xo = yo = 0
         for _ in range(layers):
             probs = []
             for _, K, N in SHAPES:
@@ -235,8 +243,10 @@ class GemvW4A16(Workload):
                                        generator=self.gen)
                 scales = (torch.rand(N, K // GROUP, device=dev, generator=self.gen) * 0.018
                           + 0.002).half()
-                x = torch.randn(1, K, device=dev, generator=self.gen).bfloat16()
-                y = torch.empty(1, N, dtype=torch.float32, device=dev)
+                x = self.x_all[xo:xo + K].view(1, K)
+                y = self.y_all[yo:yo + N].view(1, N)
+                xo += K
+                yo += N
                 probs.append((packed, scales, x, y, N, K))
             arr = (kc_lib.W4A16Problem * 4)(*[
                 kc_lib.W4A16Problem(p.data_ptr(), s.data_ptr(), x.data_ptr(), y.data_ptr(), N, K)
@@ -258,27 +268,17 @@ class GemvW4A16(Workload):
                       f"{self.work_per_step() / 1e9:.2f} GB per step"}
 
     def e2e_prepare(self):
-        t = self.torch
-        self.h_x = [[t.empty_like(x, device="cpu").pin_memory() for _, _, x, _, _, _ in probs]
-                    for probs, _ in self.layers]
-        self.h_y = [[t.empty_like(y, device="cpu").pin_memory() for _, _, _, y, _, _ in probs]
-                    for probs, _ in self.layers]
-        for li, (probs, _) in enumerate(self.layers):
-            for j, (_, _, x, _, _, _) in enumerate(probs):
-                self.h_x[li][j].copy_(x)
-        h2d = sum(x.numel() * x.element_size() for probs, _ in self.layers
-                  for _, _, x, _, _, _ in probs)
-        d2h = sum(y.numel() * y.element_size() for probs, _ in self.layers
-                  for _, _, _, y, _, _ in probs)
-        return h2d, d2h
+        self.h_x = self.x_all.cpu().pin_memory()
+        self.h_y = self.torch.empty(self.y_all.shape, dtype=self.y_all.dtype).pin_memory()
+        return (self.h_x.numel() * self.h_x.element_size(),
+                self.h_y.numel() * self.h_y.element_size())
 
     def e2e_step(self):
-        for li, (probs, arr) in enumerate(self.layers):
-            for j, (_, _, x, _, _, _) in enumerate(probs):
-                x.copy_(self.h_x[li][j], non_blocking=True)
+        # every layer's activations in, the 32 grouped launches, every output out
+        self.x_all.copy_(self.h_x, non_blocking=True)
+        for _, arr in self.layers:
             self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, self.s_ptr))
-            for j, (_, _, _, y, _, _) in enumerate(probs):
-                self.h_y[li][j].copy_(y, non_blocking=True)
+        self.h_y.copy_(self.y_all, non_blocking=True)
 
     @staticmethod
     def cpu_sample():

@@ -293,12 +293,12 @@ __device__ __forceinline__ void chunk_mma(const uint4& WA, const uint4& WB, cons
 // is loaded from global memory, permuted to fragment order, and within each
 // 128-k chunk the sixteen blocks b = 4t + j (k = 32t + 8j) move to position
 // 4j + t, so a lane's LDS.128 for word j hits 16 consecutive bytes per t.  The
-// same pass forms the per-chunk offsets sx[c][m] = -136 * sum x (fp32, the seed
-// of the chunk's MMA accumulator): a chunk's 16 blocks
-// belong to 16 consecutive lanes of one warp.  Work is handed out in units of
-// 32 blocks, one per lane, and every warp loads U units before it processes
-// any, so the loads of a warp are in flight together.  Plain loads rather than
-// a bulk copy: a bulk copy queues behind the weight tiles the CTA has already
+// same pass forms the per-chunk offsets sx[c][m] = -136 * sum x (fp32, the
+// seed of the chunk's MMA accumulator): a chunk's 16 blocks belong to 16
+// consecutive lanes of one warp.  Work is handed out in units of 32 blocks,
+// one per lane, and every warp loads U units before it processes any, so the
+// loads of a warp are in flight together.  Plain loads rather than a bulk
+// copy: a bulk copy queues behind the weight tiles the CTA has already
 // requested and lands later.
 template <int NT>
 __device__ __forceinline__ void stage_activations(const Params& P, uint8_t* xs, float* sx) {
@@ -326,10 +326,8 @@ __device__ __forceinline__ void stage_activations(const Params& P, uint8_t* xs, 
                 pis[b] = pi;
                 ms[b] = u / per;
                 kbs[b] = (u % per) * 32 + lane;
-                v[b] = kbs[b] < (P.p[pi].K >> 3)
-                           ? __ldcg(reinterpret_cast<const uint4*>(P.p[pi].x + (size_t)ms[b] * P.p[pi].K) +
-                                    kbs[b])
-                           : make_uint4(0, 0, 0, 0);
+                const uint4* xrow = reinterpret_cast<const uint4*>(P.p[pi].x + (size_t)ms[b] * P.p[pi].K);
+                v[b] = kbs[b] < (P.p[pi].K >> 3) ? __ldcg(xrow + kbs[b]) : make_uint4(0, 0, 0, 0);
             }
         }
 #pragma unroll

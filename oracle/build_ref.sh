@@ -1,10 +1,11 @@
 #!/usr/bin/env bash
 # Compiles the reference's own hot-path CUDA sources, where they lie, into
-# oracle/_ref/libkcref.so (git-ignored; travels to the GPU box as a built file).
+# oracle/_ref/libkcref.so (git-ignored; shipped with the tree as a built file).
 # TEST INFRASTRUCTURE ONLY: the parity tests load it as a second, independent
 # oracle on the B200.  Nothing is copied out of the reference tree.
 #
-#   KC_REF_DIR  reference checkout (default /root/reference); skipped if absent.
+#   KC_REF_DIR  reference checkout (default: the build machine's mount point,
+#               below); the step is skipped where no checkout exists.
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 REF="${KC_REF_DIR:-/root/reference}"

@@ -64,6 +64,53 @@ def barrier_on_stream(group=None) -> None:
     dist.all_reduce(flag, group=group)
 
 
+def check_operand(t: torch.Tensor, name: str, shape, dtypes, cuda: bool = True) -> None:
+    """Raise ValueError unless t is a contiguous tensor of the given shape and
+    one of the given dtypes (on a CUDA device when cuda): the kernels receive
+    raw pointers and sizes, so a mismatched shard would be read out of
+    bounds instead of failing."""
+    if not isinstance(t, torch.Tensor):
+        raise ValueError(f"{name}: expected a torch.Tensor, got {type(t).__name__}")
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name}: shape {tuple(t.shape)}, expected {tuple(shape)}")
+    if t.dtype not in dtypes:
+        raise ValueError(f"{name}: dtype {t.dtype}, expected one of {[str(d) for d in dtypes]}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name}: must be contiguous")
+    if cuda and not t.is_cuda:
+        raise ValueError(f"{name}: must be on a CUDA device")
+
+
+_BF16 = (torch.bfloat16, torch.int16)         # bf16 bits may arrive as int16
+_F16 = (torch.float16, torch.int16)
+_U8 = (torch.uint8,)
+_I8 = (torch.int8, torch.uint8)
+
+
+def check_col_parallel_w4a16(M, K, n_shard, gs, x, packed_shard, scales_shard, cuda=True):
+    check_operand(x, "x", (M, K), _BF16, cuda)
+    check_operand(packed_shard, "packed_shard", (n_shard, K // 2), _U8, cuda)
+    check_operand(scales_shard, "scales_shard", (n_shard, K // gs), _F16, cuda)
+
+
+def check_row_parallel_fp8(M, N, a_codes_shard, sa, w_codes_shard, sw, cuda=True):
+    if a_codes_shard.dim() != 2:
+        raise ValueError("a_codes_shard must be 2-D")
+    kr = a_codes_shard.shape[1]
+    check_operand(a_codes_shard, "a_codes_shard", (M, kr), _I8, cuda)
+    check_operand(w_codes_shard, "w_codes_shard", (N, kr), _I8, cuda)
+    check_operand(sa, "sa", (M,), (torch.float32,), cuda)
+    check_operand(sw, "sw", (N,), (torch.float32,), cuda)
+
+
+def check_mlp_block_w4a16(M, H, i_shard, gs, x, w1_packed, w1_scales, w2_packed, w2_scales, cuda=True):
+    check_operand(x, "x", (M, H), _BF16, cuda)
+    check_operand(w1_packed, "w1_packed", (i_shard, H // 2), _U8, cuda)
+    check_operand(w1_scales, "w1_scales", (i_shard, H // gs), _F16, cuda)
+    check_operand(w2_packed, "w2_packed", (H, i_shard // 2), _U8, cuda)
+    check_operand(w2_scales, "w2_scales", (H, i_shard // gs), _F16, cuda)
+
+
 class PeerBarrier:
     """Stream-ordered barrier over peer memory (kc_peer_barrier): a one-warp
     kernel per rank exchanges an increasing epoch through flag arrays shared
@@ -181,6 +228,7 @@ class ColParallelW4A16:
     def launch(self, x: torch.Tensor, packed_shard: torch.Tensor, scales_shard: torch.Tensor) -> None:
         """The fused GEMM alone (no barrier): for timing and for callers that
         synchronize the ranks themselves."""
+        check_col_parallel_w4a16(self.M, self.K, self.n_shard, self.gs, x, packed_shard, scales_shard)
         check(lib().kc_gemm_w4a16_allgather(
             ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(packed_shard.data_ptr()),
             ctypes.c_void_p(scales_shard.data_ptr()), self._outs, self.world, self.rank, self.M,
@@ -235,6 +283,7 @@ class RowParallelFP8:
         """entry_barrier: wait until no rank still reads the previous call's
         partials or output; back-to-back calls whose ranks touch neither in
         between may skip it (the previous exit barrier orders them)."""
+        check_row_parallel_fp8(self.M, self.N, a_codes_shard, sa, w_codes_shard, sw)
         Kr = a_codes_shard.shape[1]
         l = lib()
         if self.reduce == "nccl":   # GEMM into the local output, NCCL sums in place
@@ -265,6 +314,9 @@ def row_parallel_fp8(a_codes_shard: torch.Tensor, sa: torch.Tensor, w_codes_shar
     kc_gemm_fp8 into `out` and summed in place by an NCCL all-reduce."""
     M, Kr = a_codes_shard.shape
     N = w_codes_shard.shape[0]
+    check_row_parallel_fp8(M, N, a_codes_shard, sa, w_codes_shard, sw)
+    if tuple(out.shape) != (M, N) or out.dtype != torch.bfloat16 or out.stride(1) != 1 or not out.is_cuda:
+        raise ValueError(f"out: expected a CUDA bf16 [{M}, {N}] tensor with unit column stride")
     check(lib().kc_gemm_fp8(ctypes.c_void_p(a_codes_shard.data_ptr()), ctypes.c_void_p(sa.data_ptr()),
                             ctypes.c_void_p(w_codes_shard.data_ptr()), ctypes.c_void_p(sw.data_ptr()),
                             ctypes.c_void_p(out.data_ptr()), 0, M, N, Kr, out.stride(0), _stream()))
@@ -324,6 +376,8 @@ class MLPBlockW4A16:
 
     def launch(self, x, w1_packed, w1_scales, w2_packed, w2_scales) -> None:
         """Both GEMMs of this rank (no collective): for timing."""
+        check_mlp_block_w4a16(self.M, self.H, self.i_shard, self.gs, x, w1_packed, w1_scales,
+                              w2_packed, w2_scales)
         l = lib()
         check(l.kc_gemm_w4a16_act(
             ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(w1_packed.data_ptr()),

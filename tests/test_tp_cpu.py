@@ -132,3 +132,34 @@ def test_w4_shard_helpers():
     assert shard_w4_cols(packed, scales, 64, 4, 3)[1].shape == (8, 1)   # K shard 64: one group
     with pytest.raises(ValueError):
         shard_w4_cols(packed, scales, 64, 8, 0)      # K shard 32 would split a scale group
+
+
+def test_driver_operand_checks():
+    """The tensor-parallel drivers refuse mismatched shards on the host (the
+    kernels would read them out of bounds); shown with CPU tensors, cuda=False."""
+    import tp
+    M, H, I, gs = 8, 256, 512, 128
+    x = torch.zeros(M, H, dtype=torch.bfloat16)
+    ok = dict(w1_packed=torch.zeros(I, H // 2, dtype=torch.uint8),
+              w1_scales=torch.zeros(I, H // gs, dtype=torch.float16),
+              w2_packed=torch.zeros(H, I // 2, dtype=torch.uint8),
+              w2_scales=torch.zeros(H, I // gs, dtype=torch.float16))
+    tp.check_mlp_block_w4a16(M, H, I, gs, x, cuda=False, **ok)
+    for key, bad in [("w1_packed", torch.zeros(I // 2, H // 2, dtype=torch.uint8)),    # half the rows
+                     ("w2_packed", torch.zeros(H, I, dtype=torch.uint8)),              # unpacked
+                     ("w1_scales", torch.zeros(I, H // gs, dtype=torch.float32)),      # fp32 scales
+                     ("w2_scales", torch.zeros(I // gs, H, dtype=torch.float16).t())]: # transposed view
+        with pytest.raises(ValueError, match=key):
+            tp.check_mlp_block_w4a16(M, H, I, gs, x, cuda=False, **{**ok, key: bad})
+    with pytest.raises(ValueError, match="CUDA"):
+        tp.check_mlp_block_w4a16(M, H, I, gs, x, **ok)
+    p = torch.zeros(64, H // 2, dtype=torch.uint8)
+    s = torch.zeros(64, H // gs, dtype=torch.float16)
+    tp.check_col_parallel_w4a16(M, H, 64, gs, x, p, s, cuda=False)
+    with pytest.raises(ValueError, match="x"):
+        tp.check_col_parallel_w4a16(M, H, 64, gs, x.float(), p, s, cuda=False)
+    a = torch.zeros(M, 128, dtype=torch.int8)
+    w = torch.zeros(32, 128, dtype=torch.int8)
+    tp.check_row_parallel_fp8(M, 32, a, torch.zeros(M), w, torch.zeros(32), cuda=False)
+    with pytest.raises(ValueError, match="w_codes_shard"):
+        tp.check_row_parallel_fp8(M, 32, a, torch.zeros(M), w[:, :64], torch.zeros(32), cuda=False)

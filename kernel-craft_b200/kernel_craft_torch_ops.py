@@ -56,6 +56,45 @@ def _require_cuda(*ts: torch.Tensor) -> None:
             raise ValueError("kernel-craft ops take CUDA tensors only (no CPU path)")
 
 
+def _expect(t: torch.Tensor, name: str, numel=None, shape=None, dtypes=None) -> None:
+    """Raise ValueError unless t has the element count / shape / dtype the
+    kernel will read: the library receives raw pointers and sizes, so a short
+    or mistyped tensor would be read out of bounds instead of failing."""
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name}: shape {tuple(t.shape)}, expected {tuple(shape)}")
+    if numel is not None and t.numel() < numel:
+        raise ValueError(f"{name}: {t.numel()} elements, the kernel reads {numel}")
+    if dtypes is not None and t.dtype not in dtypes:
+        raise ValueError(f"{name}: dtype {t.dtype}, expected one of {[str(d) for d in dtypes]}")
+
+
+_F32 = (torch.float32,)
+_F16 = (torch.float16, torch.int16)      # fp16 bits may arrive as int16
+_BF16 = (torch.bfloat16, torch.int16)
+_U8 = (torch.uint8, torch.int8)
+_I8 = (torch.int8, torch.uint8)
+
+
+def _check_int4_ref(packed, scales, zeros, rows, cols, group_size):
+    if rows < 0 or cols < 0 or group_size <= 0:
+        raise ValueError("rows, cols must be >= 0 and group_size > 0")
+    g = -(-cols // group_size)
+    _expect(packed, "packed", numel=rows * ((cols + 1) // 2), dtypes=_U8)
+    _expect(scales, "scales", numel=rows * g, dtypes=_F32)
+    # the reference kernel's zero-point row stride is floor(G/2) bytes
+    # (quant_int4.cu:93); an odd group count reads one byte past the last row
+    _expect(zeros, "zeros", numel=(rows * (g // 2) + g % 2) if rows else 0, dtypes=_U8)
+
+
+def _check_w4(packed, scales, group_size, name=""):
+    if packed.dim() != 2 or group_size <= 0 or (packed.shape[1] * 2) % group_size:
+        raise ValueError(f"{name}packed must be [N, K/2] with group_size dividing K")
+    n, k = packed.shape[0], packed.shape[1] * 2
+    _expect(packed, name + "packed", dtypes=_U8)
+    _expect(scales, name + "scales_f16", shape=(n, k // group_size), dtypes=_F16)
+    return n, k
+
+
 # ---------------------------------------------------------------------------
 # Reference operators (kernel_craft_torch_ops.py:265-381)
 # ---------------------------------------------------------------------------
@@ -64,6 +103,7 @@ def int4_dequantize(packed, scales, zeros, rows: int, cols: int, group_size: int
     """INT4 -> fp32 [rows, cols]; reference semantics (sign-extended nibbles,
     unsigned zero points)."""
     packed, scales, zeros = packed.contiguous(), scales.contiguous(), zeros.contiguous()
+    _check_int4_ref(packed, scales, zeros, rows, cols, group_size)
     _require_cuda(packed, scales, zeros)
     out = torch.empty(rows, cols, dtype=torch.float32, device=packed.device)
     check(lib().kc_dequantize_int4_f32(_ptr(packed), _ptr(scales), _ptr(zeros), _ptr(out),
@@ -74,6 +114,8 @@ def int4_dequantize(packed, scales, zeros, rows: int, cols: int, group_size: int
 def int4_gemv(packed, scales, zeros, x, rows: int, cols: int, group_size: int = 128):
     """y[rows] = W_int4 . x in fp32 (on-the-fly dequant)."""
     packed, scales, zeros, x = (t.contiguous() for t in (packed, scales, zeros, x))
+    _check_int4_ref(packed, scales, zeros, rows, cols, group_size)
+    _expect(x, "x", numel=cols, dtypes=_F32)
     _require_cuda(packed, scales, zeros, x)
     y = torch.empty(rows, dtype=torch.float32, device=packed.device)
     with kernel_span("int4_gemv", rows=rows, cols=cols, group_size=group_size):
@@ -85,6 +127,9 @@ def int4_gemv(packed, scales, zeros, x, rows: int, cols: int, group_size: int = 
 def fp8_quantize(x, per_token: bool = True) -> Tuple[torch.Tensor, torch.Tensor]:
     """fp32 [rows, cols] -> (int8 E4M3 codes [rows, cols], fp32 scales [rows] or [1])."""
     x = x.contiguous()
+    if x.dim() != 2:
+        raise ValueError("x must be 2-D [rows, cols]")
+    _expect(x, "x", dtypes=_F32)
     _require_cuda(x)
     rows, cols = x.shape
     q = torch.empty(rows, cols, dtype=torch.int8, device=x.device)
@@ -104,6 +149,8 @@ def fp8_quantize(x, per_token: bool = True) -> Tuple[torch.Tensor, torch.Tensor]
 def fp8_dequantize(q, scales, rows: int, cols: int, per_token: bool = True):
     """int8 E4M3 codes -> fp32 [rows, cols]."""
     q, scales = q.contiguous(), scales.contiguous()
+    _expect(q, "q", numel=rows * cols, dtypes=_I8)
+    _expect(scales, "scales", numel=rows if per_token else 1, dtypes=_F32)
     _require_cuda(q, scales)
     out = torch.empty(rows, cols, dtype=torch.float32, device=q.device)
     check(lib().kc_dequantize_fp8(_ptr(q), _ptr(scales), _ptr(out), rows, cols, per_token,
@@ -118,6 +165,10 @@ def fp8_dequantize(q, scales, rows: int, cols: int, per_token: bool = True):
 def smoothquant_scale(x, smooth):
     """x[r, c] / smooth[c] (fp8_quant.cu:174-184 semantics)."""
     x, smooth = x.contiguous(), smooth.contiguous()
+    if x.dim() != 2:
+        raise ValueError("x must be 2-D [rows, cols]")
+    _expect(x, "x", dtypes=_F32)
+    _expect(smooth, "smooth", numel=x.shape[1], dtypes=_F32)
     _require_cuda(x, smooth)
     rows, cols = x.shape
     out = torch.empty_like(x)
@@ -128,6 +179,10 @@ def smoothquant_scale(x, smooth):
 def smoothquant_fp8_quantize(x, smooth) -> Tuple[torch.Tensor, torch.Tensor]:
     """Fused SmoothQuant divide + per-token FP8 quantization."""
     x, smooth = x.contiguous(), smooth.contiguous()
+    if x.dim() != 2:
+        raise ValueError("x must be 2-D [rows, cols]")
+    _expect(x, "x", dtypes=_F32)
+    _expect(smooth, "smooth", numel=x.shape[1], dtypes=_F32)
     _require_cuda(x, smooth)
     rows, cols = x.shape
     q = torch.empty(rows, cols, dtype=torch.int8, device=x.device)
@@ -140,6 +195,9 @@ def smoothquant_fp8_quantize(x, smooth) -> Tuple[torch.Tensor, torch.Tensor]:
 def fp8_quantize_per_channel(w) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per-output-channel weight quantization of W[N, K]: one scale per row."""
     w = w.contiguous()
+    if w.dim() != 2:
+        raise ValueError("w must be 2-D [N, K]")
+    _expect(w, "w", dtypes=_F32)
     _require_cuda(w)
     n, k = w.shape
     q = torch.empty(n, k, dtype=torch.int8, device=w.device)
@@ -151,8 +209,8 @@ def fp8_quantize_per_channel(w) -> Tuple[torch.Tensor, torch.Tensor]:
 def w4a16_dequantize(packed, scales_f16, group_size: int = 128):
     """GPTQ W4 (implicit zero-point 8, fp16 scales) -> bf16 [N, K]."""
     packed, scales_f16 = packed.contiguous(), scales_f16.contiguous()
+    n, k = _check_w4(packed, scales_f16, group_size)
     _require_cuda(packed, scales_f16)
-    n, k = packed.shape[0], packed.shape[1] * 2
     out = torch.empty(n, k, dtype=torch.bfloat16, device=packed.device)
     check(lib().kc_dequantize_w4_bf16(_ptr(packed), _ptr(scales_f16), _ptr(out), n, k,
                                       group_size, _stream()))
@@ -162,11 +220,12 @@ def w4a16_dequantize(packed, scales_f16, group_size: int = 128):
 def w4a16_gemv(packed, scales_f16, x, group_size: int = 128):
     """y[M, N] (fp32) = x[M, K] (bf16, M <= 16) . W^T with W the GPTQ W4 [N, K]."""
     packed, scales_f16, x = packed.contiguous(), scales_f16.contiguous(), x.contiguous()
-    _require_cuda(packed, scales_f16, x)
     if x.dim() == 1:
         x = x.unsqueeze(0)
-    m, k = x.shape
-    n = packed.shape[0]
+    n, k = _check_w4(packed, scales_f16, group_size)
+    _expect(x, "x", shape=(x.shape[0], k), dtypes=_BF16)
+    _require_cuda(packed, scales_f16, x)
+    m = x.shape[0]
     y = torch.empty(m, n, dtype=torch.float32, device=packed.device)
     with kernel_span("w4a16_gemv", rows=n, cols=k, batch=m, group_size=group_size):
         check(lib().kc_gemv_w4a16(_ptr(packed), _ptr(scales_f16), _ptr(x), _ptr(y), m, n, k,
@@ -179,23 +238,27 @@ def w4a16_gemv_grouped(problems: Sequence[Tuple[torch.Tensor, torch.Tensor, torc
     """One launch over several (packed, scales_f16, x) problems sharing M."""
     if not 1 <= len(problems) <= kc_lib.KC_W4A16_MAX_PROBLEMS:
         raise ValueError("1..8 problems per grouped launch")
-    arr = (kc_lib.W4A16Problem * len(problems))()
-    outs, keep = [], []
+    # every problem is checked before any is handed to the library
+    checked = []
     m = None
     for i, (packed, scales, x) in enumerate(problems):
         packed, scales, x = packed.contiguous(), scales.contiguous(), x.contiguous()
-        _require_cuda(packed, scales, x)
         if x.dim() == 1:
             x = x.unsqueeze(0)
+        n, k = _check_w4(packed, scales, group_size, name=f"problem {i}: ")
+        _expect(x, f"problem {i}: x", shape=(x.shape[0], k), dtypes=_BF16)
         m = x.shape[0] if m is None else m
         if x.shape[0] != m:
             raise ValueError("all problems of a grouped launch share M")
-        n, k = packed.shape[0], packed.shape[1] * 2
+        checked.append((packed, scales, x, n, k))
+    arr = (kc_lib.W4A16Problem * len(problems))()
+    outs = []
+    for i, (packed, scales, x, n, k) in enumerate(checked):
+        _require_cuda(packed, scales, x)
         y = torch.empty(m, n, dtype=torch.float32, device=packed.device)
         arr[i] = kc_lib.W4A16Problem(packed.data_ptr(), scales.data_ptr(), x.data_ptr(),
                                      y.data_ptr(), n, k)
         outs.append(y)
-        keep += [packed, scales, x]
     check(lib().kc_gemv_w4a16_grouped(arr, len(problems), m, group_size, _stream()))
     return outs
 
@@ -213,11 +276,14 @@ def w4a16_gemm(x, packed, scales_f16, group_size: int = 128, out_dtype=torch.bfl
     if activation not in _ACTIVATIONS:
         raise ValueError(f"activation must be one of {sorted(_ACTIVATIONS)}")
     x, packed, scales_f16 = x.contiguous(), packed.contiguous(), scales_f16.contiguous()
+    n, k = _check_w4(packed, scales_f16, group_size)
+    if x.dim() != 2 or x.shape[1] != k:
+        raise ValueError(f"x must be [M, {k}] (the packed weights' K), got {tuple(x.shape)}")
+    _expect(x, "x", dtypes=_BF16)
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out_dtype must be torch.bfloat16 or torch.float32")
     _require_cuda(x, packed, scales_f16)
-    m, k = x.shape
-    n = packed.shape[0]
-    if packed.shape[1] * 2 != k:
-        raise ValueError(f"x has K={k}, packed weights K={packed.shape[1] * 2}")
+    m = x.shape[0]
     out = torch.empty(m, n, dtype=out_dtype, device=x.device)
     with kernel_span("w4a16_gemm", rows=n, cols=k, batch=m, group_size=group_size):
         check(lib().kc_gemm_w4a16_act(_ptr(x), _ptr(packed), _ptr(scales_f16), _ptr(out),
@@ -233,9 +299,17 @@ def fp8_gemm(a_codes, sa, w_codes, sw, out_dtype=torch.bfloat16):
     bf16 (default) or fp32 output."""
     a_codes, w_codes = a_codes.contiguous(), w_codes.contiguous()
     sa, sw = sa.contiguous(), sw.contiguous()
-    _require_cuda(a_codes, sa, w_codes, sw)
+    if a_codes.dim() != 2 or w_codes.dim() != 2 or a_codes.shape[1] != w_codes.shape[1]:
+        raise ValueError("a_codes [M, K] and w_codes [N, K] must share K")
     m, k = a_codes.shape
     n = w_codes.shape[0]
+    _expect(a_codes, "a_codes", dtypes=_I8)
+    _expect(w_codes, "w_codes", dtypes=_I8)
+    _expect(sa, "sa", shape=(m,), dtypes=_F32)
+    _expect(sw, "sw", shape=(n,), dtypes=_F32)
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("out_dtype must be torch.bfloat16 or torch.float32")
+    _require_cuda(a_codes, sa, w_codes, sw)
     out = torch.empty(m, n, dtype=out_dtype, device=a_codes.device)
     with kernel_span("fp8_gemm", rows=n, cols=k, batch=m):
         check(lib().kc_gemm_fp8(_ptr(a_codes), _ptr(sa), _ptr(w_codes), _ptr(sw), _ptr(out),

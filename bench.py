@@ -253,9 +253,41 @@ class GemvW4A16(Workload):
                 for p, s, x, y, N, K in probs])
             self.layers.append((probs, arr))
 
-    def step(self):
+    use_graph = True      # replay the step's launches as one CUDA graph (--no-graph: eager)
+
+    def _launch_all(self):
+        # launched on the current stream: the capture stream inside the graph
+        # capture, the bench's stream otherwise
+        st = ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
         for _, arr in self.layers:
-            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, self.s_ptr))
+            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, st))
+
+    def _capture(self):
+        """The step's 32 grouped launches as one CUDA graph (captured after one
+        eager step, which sets the kernel attributes); eager if capture fails."""
+        torch = self.torch
+        self._launch_all()
+        torch.cuda.synchronize()
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._launch_all()
+            torch.cuda.synchronize()
+            self.graph = g
+        except RuntimeError as e:              # fall back, and say so in the config
+            self.graph = None
+            self.use_graph = False
+            self.graph_error = str(e).splitlines()[0][:200]
+
+    def step(self):
+        if not self.use_graph:
+            self._launch_all()
+            return
+        if getattr(self, "graph", None) is None:
+            self._capture()
+            if not self.use_graph:
+                return
+        self.graph.replay()
 
     def work_per_step(self):
         return layer_bytes(1) * self.n_layers
@@ -263,7 +295,11 @@ class GemvW4A16(Workload):
     def config(self):
         return {"workload": "7b-decode-linear-set-m1", "layers": self.n_layers,
                 "shapes_KN": [[K, N] for _, K, N in SHAPES], "M": 1, "group_size": GROUP,
-                "bytes_per_step": self.work_per_step(), "launch": "one grouped launch per layer",
+                "bytes_per_step": self.work_per_step(),
+                "launch": "one grouped launch per layer" + (
+                    ", the step's launches replayed as one CUDA graph" if self.use_graph else
+                    ", eager" + (f" (graph capture failed: {self.graph_error})"
+                                 if hasattr(self, "graph_error") else "")),
                 "l2": f"inputs larger than L2: {self.n_layers} distinct layers = "
                       f"{self.work_per_step() / 1e9:.2f} GB per step"}
 
@@ -276,8 +312,7 @@ class GemvW4A16(Workload):
     def e2e_step(self):
         # every layer's activations in, the 32 grouped launches, every output out
         self.x_all.copy_(self.h_x, non_blocking=True)
-        for _, arr in self.layers:
-            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, self.s_ptr))
+        self.step()
         self.h_y.copy_(self.y_all, non_blocking=True)
 
     @staticmethod
@@ -812,6 +847,8 @@ def main(argv=None) -> int:
     ap.add_argument("--workload", default="gemv", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e pass")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="gemv: launch the step eagerly instead of replaying it as a CUDA graph")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="gemv: decoder layers per step (default 32; fewer only for profiling)")
     ap.add_argument("--heat-s", type=float, default=1.5,
@@ -843,6 +880,7 @@ def main(argv=None) -> int:
     W = WORKLOADS[args.workload]
     if W is GemvW4A16:
         wl = W(torch, l, dev, s_ptr, rank, world, layers=args.layers)
+        wl.use_graph = not args.no_graph
     else:
         wl = W(torch, l, dev, s_ptr, rank, world)
     torch.cuda.synchronize()

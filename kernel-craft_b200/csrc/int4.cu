@@ -84,27 +84,47 @@ __global__ void dequant_int4_f32_vec(const uint8_t* __restrict__ packed,
     }
 }
 
-// fp32 GEMV, one warp per row.  VEC: 16-byte chunks, one group per chunk.
-template <bool VEC>
-__global__ void __launch_bounds__(256) gemv_int4_f32(const uint8_t* __restrict__ packed,
-                                                     const float* __restrict__ scales,
-                                                     const uint8_t* __restrict__ zeros,
-                                                     const float* __restrict__ x,
-                                                     float* __restrict__ y, int rows, int cols,
-                                                     int gs) {
+// fp32 GEMV over 16-byte chunks (32 weights of one group each), two rows
+// per warp so every x load serves both; a lane takes chunks lane, lane + 32,
+// ... in order and issues the packed loads of kU of them (both rows) before
+// it computes any, so a warp has 2 * kU * 512 bytes in flight instead of
+// 512.  Each row's accumulation order per lane is the one-row order, so the
+// result does not depend on the row pairing.
+__global__ void __launch_bounds__(256) gemv_int4_f32_vec(const uint8_t* __restrict__ packed,
+                                                         const float* __restrict__ scales,
+                                                         const uint8_t* __restrict__ zeros,
+                                                         const float* __restrict__ x,
+                                                         float* __restrict__ y, int rows, int cols,
+                                                         int gs) {
+    constexpr int kU = 4;
     const int lane = threadIdx.x & 31;
     const int warps = (gridDim.x * blockDim.x) >> 5;
-    const int sc = cols / gs;
-    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
-        float acc = 0.f;
-        if (VEC) {
-            const uint8_t* prow = packed + (long)r * (cols / 2);
-            for (int j = lane; j < cols / 32; j += 32) {
+    const int sc = cols / gs, cpr = cols / 32;
+    for (int r0 = 2 * ((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r0 < rows; r0 += 2 * warps) {
+        const bool two = r0 + 1 < rows;
+        const int r1 = two ? r0 + 1 : r0;     // a lone last row computes itself twice
+        const uint8_t* p0 = packed + (long)r0 * (cols / 2);
+        const uint8_t* p1 = packed + (long)r1 * (cols / 2);
+        float acc0 = 0.f, acc1 = 0.f;
+        for (int jb = lane; jb < cpr; jb += 32 * kU) {
+            uint4 v0[kU], v1[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int j = jb + 32 * u;
+                if (j < cpr) {
+                    v0[u] = kc_ldg_stream(p0 + 16 * j);
+                    v1[u] = kc_ldg_stream(p1 + 16 * j);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int j = jb + 32 * u;
+                if (j >= cpr) break;
                 const int g = (32 * j) / gs;
-                const float s = scales[(long)r * sc + g];
-                const int zp = ref_zp(zeros, r, cols, gs, g);
-                const uint4 v = kc_ldg_stream(prow + 16 * j);
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                const float s0 = scales[(long)r0 * sc + g], s1 = scales[(long)r1 * sc + g];
+                const int z0 = ref_zp(zeros, r0, cols, gs, g), z1 = ref_zp(zeros, r1, cols, gs, g);
+                const uint32_t w0[4] = {v0[u].x, v0[u].y, v0[u].z, v0[u].w};
+                const uint32_t w1[4] = {v1[u].x, v1[u].y, v1[u].z, v1[u].w};
                 const float4* xv = reinterpret_cast<const float4*>(x + 32 * j);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -112,24 +132,45 @@ __global__ void __launch_bounds__(256) gemv_int4_f32(const uint8_t* __restrict__
                     const float xe[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
-                        const float wv = (float)(sx4((w[q] >> (4 * e)) & 15u) - zp) * s;
-                        acc = fmaf(wv, xe[e], acc);
+                        acc0 = fmaf((float)(sx4((w0[q] >> (4 * e)) & 15u) - z0) * s0, xe[e], acc0);
+                        acc1 = fmaf((float)(sx4((w1[q] >> (4 * e)) & 15u) - z1) * s1, xe[e], acc1);
                     }
                 }
             }
-        } else {
-            for (int b = lane; 2 * b < cols; b += 32) {
-                const int c0 = 2 * b, c1 = c0 + 1;
-                const uint8_t p = packed[(long)r * (cols / 2) + b];
-                const int g0 = c0 / gs, g1 = c1 / gs;
-                const float w0 = (float)(sx4(p & 15u) - ref_zp(zeros, r, cols, gs, g0)) *
-                                 scales[(long)r * sc + g0];
-                acc = fmaf(w0, x[c0], acc);
-                if (c1 < cols) {
-                    const float w1 = (float)(sx4(p >> 4) - ref_zp(zeros, r, cols, gs, g1)) *
-                                     scales[(long)r * sc + g1];
-                    acc = fmaf(w1, x[c1], acc);
-                }
+        }
+        acc0 = kc_warp_sum(acc0);
+        acc1 = kc_warp_sum(acc1);
+        if (lane == 0) {
+            y[r0] = acc0;
+            if (two) y[r1] = acc1;
+        }
+    }
+}
+
+// fp32 GEMV, one warp per row, one packed byte per lane and step: any shape
+// (odd group sizes, cols not a multiple of 32, unaligned pointers).
+__global__ void __launch_bounds__(256) gemv_int4_f32_bytes(const uint8_t* __restrict__ packed,
+                                                           const float* __restrict__ scales,
+                                                           const uint8_t* __restrict__ zeros,
+                                                           const float* __restrict__ x,
+                                                           float* __restrict__ y, int rows, int cols,
+                                                           int gs) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    const int sc = cols / gs;
+    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+        float acc = 0.f;
+        for (int b = lane; 2 * b < cols; b += 32) {
+            const int c0 = 2 * b, c1 = c0 + 1;
+            const uint8_t p = packed[(long)r * (cols / 2) + b];
+            const int g0 = c0 / gs, g1 = c1 / gs;
+            const float w0 = (float)(sx4(p & 15u) - ref_zp(zeros, r, cols, gs, g0)) *
+                             scales[(long)r * sc + g0];
+            acc = fmaf(w0, x[c0], acc);
+            if (c1 < cols) {
+                const float w1 = (float)(sx4(p >> 4) - ref_zp(zeros, r, cols, gs, g1)) *
+                                 scales[(long)r * sc + g1];
+                acc = fmaf(w1, x[c1], acc);
             }
         }
         acc = kc_warp_sum(acc);
@@ -237,11 +278,13 @@ int kc_gemv_int4_f32(const uint8_t* packed, const float* scales, const uint8_t* 
     if (rows == 0) return KC_OK;
     const bool vec = (cols % 32 == 0) && (gs % 32 == 0) && kc::aligned(packed, 16) &&
                      kc::aligned(x, 16);
+    if (vec) {
+        const int grid2 = grid_for(((long)rows + 15) / 16, 256);   // 8 warps x 2 rows per CTA
+        gemv_int4_f32_vec<<<grid2, 256, 0, stream>>>(packed, scales, zeros, x, y, rows, cols, gs);
+        return kc::check_launch("gemv_int4_f32");
+    }
     const int grid = grid_for(((long)rows + 7) / 8, 256);
-    if (vec)
-        gemv_int4_f32<true><<<grid, 256, 0, stream>>>(packed, scales, zeros, x, y, rows, cols, gs);
-    else
-        gemv_int4_f32<false><<<grid, 256, 0, stream>>>(packed, scales, zeros, x, y, rows, cols, gs);
+    gemv_int4_f32_bytes<<<grid, 256, 0, stream>>>(packed, scales, zeros, x, y, rows, cols, gs);
     return kc::check_launch("gemv_int4_f32");
 }
 

@@ -638,7 +638,7 @@ class GemvInt4(Workload):
     dtype = "f32"
     data = ("synthetic (uniform nibbles, packed^0x88 with zero points 0, fp32 scales "
             "U[0.002,0.02], fp32 x N(0,1))")
-    kernel = "gemv_int4_f32"
+    kernel = "gemv_int4_f32_vec"
     profile = "gemv_int4_f32_4096x4096"
     R = C = 4096
     COPIES = 32   # 32 x 9 MB = 288 MB of distinct weights rotate through L2

@@ -270,7 +270,9 @@ class GemvW4A16(Workload):
         torch.cuda.synchronize()
         try:
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            # thread_local: other threads (e.g. the NCCL watchdog of a
+            # multi-rank run) keep their CUDA calls legal during the capture
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
                 self._launch_all()
             torch.cuda.synchronize()
             self.graph = g

@@ -7,7 +7,6 @@ are the parity tests: they call the CUDA library through its C ABI and compare
 with the oracle (and, when oracle/_ref/libkcref.so is present, with the
 reference's own kernels run on the same inputs).
 """
-import os
 import sys
 from pathlib import Path
 

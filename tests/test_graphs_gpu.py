@@ -4,7 +4,6 @@ W4A16 and FP8 GEMMs, and the MLP block, captured once with torch.cuda.graph
 and replayed with new activations copied into the captured input buffers.
 Every replay must equal an eager run of the same launches bit for bit (same
 kernels, same inputs), and no device-side wait may give up."""
-import numpy as np
 import pytest
 import torch
 

@@ -1,37 +1,49 @@
 """bench.py -- benchmarks of the B200 quantized-linear library.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kc|reference]
-                    [--workload gemv|gemm_w4a16|gemm_fp8|quant_fp8|gemv_int4|mlp_w4a16]
+                    [--workload all|gemv|gemm_w4a16|gemm_fp8|quant_fp8|gemv_int4|mlp_w4a16]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
 
-Default workload ("gemv", BASELINE config 2, the metric "W4A16 GEMV HBM
-GB/s"): the Llama-style 7B decode linear set at batch M = 1 -- per layer the
-K->N projections 4096->12288 (QKV), 4096->4096 (O), 4096->22016 (gate+up) and
-11008->4096 (down); GPTQ INT4 weights (uniform nibbles, implicit zero-point 8,
-group 128, fp16 scales U[0.002, 0.02]); bf16 activations N(0,1); fp32
-accumulation and output.  One step = one decode token through a 32-layer
-stack: 32 launches (one grouped launch of a layer's four projections each),
-3.35 GB of distinct weights per step, so no step reads weights from L2
-(126 MB).  value = algorithmic bytes per step / device time per step.
+With no --workload (``all``) one JSON line is printed per workload, in the
+order gemv_int4, quant_fp8, gemm_w4a16, gemm_fp8, and last the headline
+decode-GEMV line ("W4A16 GEMV HBM GB/s"):
 
-Other workloads (one line each, same keys):
-  gemm_w4a16  config 3: W4A16 GEMM M=2048, K=8192, N=28672, group 128, bf16 out
-  gemm_fp8    config 4: FP8 W8A8 GEMM M=4096, K=8192, N=8192, per-token x
-              per-channel scales, bf16 out
-  quant_fp8   config 1: per-token FP8 quantization of fp32 x [8192, 8192]
-              with 1 % outlier channels (x20)
-  gemv_int4   config 0: the reference ABI's fp32 INT4 GEMV, 4096 x 4096
+  gemv        the Llama-style 7B decode linear set at batch M = 1 -- per
+              layer the K->N projections 4096->12288 (QKV), 4096->4096 (O),
+              4096->22016 (gate+up) and 11008->4096 (down); GPTQ INT4 weights
+              (uniform nibbles, implicit zero-point 8, group 128, fp16 scales
+              U[0.002, 0.02]); bf16 activations N(0,1); fp32 accumulation and
+              output.  One step = one decode token through a 32-layer stack:
+              32 launches (one grouped launch of a layer's four projections
+              each), 3.35 GB of distinct weights per step, so no step reads
+              weights from L2 (126 MB).  value = algorithmic bytes per step /
+              device time per step.  At N > 1 every GPU runs its own replica
+              (a decode GEMV has nothing to exchange at M = 1).
+  gemm_w4a16  W4A16 GEMM M=2048, K=8192, N=28672, group 128, bf16 out; at
+              N > 1 column parallel (N split, the all-gather fused into the
+              GEMM epilogue), strong scaling
+  gemm_fp8    FP8 W8A8 GEMM M=4096, K=8192, N=8192, per-token x per-channel
+              scales, bf16 out; at N > 1 row parallel (K split, bf16 sum of
+              the partials), strong scaling
+  quant_fp8   per-token FP8 quantization of fp32 x [8192, 8192] with 1 %
+              outlier channels (x20)
+  gemv_int4   the reference ABI's fp32 INT4 GEMV, 4096 x 4096
   mlp_w4a16   the reference's MLP block (col-parallel linear -> GELU ->
               row-parallel linear -> all-reduce) on W4A16 weights, M=2048,
               H=4096, I=16384, GELU in the first GEMM's epilogue, fp32 out
+              (run with --workload mlp_w4a16)
 
-At N > 1 every rank runs the same workload on its own GPU (replicas; a decode
-GEMV does not shard usefully at M = 1) and value is the aggregate.
+At N > 1 the sharded GEMMs first pass a correctness gate: the sharded result
+on a small problem is compared with the single-GPU kernel's on the same
+inputs (bit-equal for the column-parallel GEMM, normwise <= 1e-2 for the
+row-parallel one, whose bf16 partials are rounded before the sum); a
+mismatch ends the run with exit code 3 before anything is timed.
 
 The reference arm (--impl reference) times the reference path's CPU
 restatement (oracle/, "kind": "port" -- the reference ships no CPU
 implementation of this path, only CUDA kernels) on the host cores, one
-bounded sample of the workload per step.
+bounded sample of the workload per step, and prints the same sequence of
+lines.
 """
 from __future__ import annotations
 
@@ -167,6 +179,7 @@ class Workload:
     """One benchmark case.  Subclasses fill the device buffers in __init__(),
     launch one step in step() and describe the algorithmic work per step."""
     name = ""
+    workload_id = ""       # the config name both arms report
     metric = ""
     unit = "GB/s"
     bound = "hbm"          # or "tensor-bf16" / "tensor-fp8"
@@ -212,9 +225,24 @@ class Workload:
         """(fn, work per call in metric units * 1/scale, sample description)"""
         raise NotImplementedError
 
+    def gate(self):
+        """Multi-GPU correctness gate, run on every rank before anything is
+        timed: (ok, record).  Workloads without an exchange have none."""
+        return True, None
+
+    def close(self):
+        """Releases what the workload shares with the other ranks."""
+
+
+def _normwise(a, b) -> float:
+    """max |a - b| / max |b| over two tensors (on the device)."""
+    d = (a.double() - b.double()).abs().max()
+    return float(d / b.double().abs().max().clamp_min(1e-30))
+
 
 class GemvW4A16(Workload):
     name = "gemv"
+    workload_id = "7b-decode-linear-set-m1"
     metric = "W4A16 GEMV HBM GB/s (7B decode linear set, M=1)"
     dtype = "bf16"
     data = "synthetic (seeded uniform INT4 nibbles, fp16 scales U[0.002,0.02], bf16 N(0,1))"
@@ -295,7 +323,7 @@ class GemvW4A16(Workload):
         return layer_bytes(1) * self.n_layers
 
     def config(self):
-        return {"workload": "7b-decode-linear-set-m1", "layers": self.n_layers,
+        return {"workload": self.workload_id, "layers": self.n_layers,
                 "shapes_KN": [[K, N] for _, K, N in SHAPES], "M": 1, "group_size": GROUP,
                 "bytes_per_step": self.work_per_step(),
                 "launch": "one grouped launch per layer" + (
@@ -331,21 +359,26 @@ class GemvW4A16(Workload):
 
     @staticmethod
     def reference_step():
+        # the kc arm's step: 32 distinct layers (3.35 GB of weights, more than
+        # any host cache), one decode token through all of them
         O = _oracle()
         probs = []
-        for i, (_, K, N) in enumerate(SHAPES):
-            packed, scales = O.make_w4_gptq(N, K, GROUP, seed=10 + i)
-            x = O.make_activations_bf16(1, K, seed=20 + i)
-            probs.append((packed, scales, x, N, K))
+        for layer in range(LAYERS):
+            for i, (_, K, N) in enumerate(SHAPES):
+                packed, scales = O.make_w4_gptq(N, K, GROUP, seed=1000 + 8 * layer + i)
+                x = O.make_activations_bf16(1, K, seed=2000 + 8 * layer + i)
+                probs.append((packed, scales, x, N, K))
 
         def fn():
             for packed, scales, x, N, K in probs:
                 O.gemv_w4a16(packed, scales, x, 1, N, K, GROUP)
-        return fn, layer_bytes(1), "one layer (4 projections, 104.6 MB INT4) per step"
+        return fn, layer_bytes(1) * LAYERS, \
+            f"the full step: {LAYERS} distinct layers of 4 projections (3.35 GB INT4), M=1"
 
 
 class GemmW4A16(Workload):
     name = "gemm_w4a16"
+    workload_id = "w4a16-gemm-2048x28672x8192"
     metric = "W4A16 GEMM TFLOP/s (M=2048, K=8192, N=28672, group 128)"
     unit = "TFLOP/s"
     bound = "tensor-bf16"
@@ -405,7 +438,7 @@ class GemmW4A16(Workload):
                 "over NVLink (fused all-gather), one peer-flag barrier per step")
 
     def config(self):
-        return {"workload": "w4a16-gemm-2048x28672x8192", "M": self.M, "N": self.N, "K": self.K,
+        return {"workload": self.workload_id, "M": self.M, "N": self.N, "K": self.K,
                 "group_size": GROUP, "out": "bf16",
                 "l2": f"{self.COPIES} rotating operand sets, each step also writes the full "
                       "117 MB output (larger than L2)"}
@@ -447,9 +480,41 @@ class GemmW4A16(Workload):
         fn, flops = cls._cpu(8)
         return fn, flops, "8 of 2048 token rows x all 28672 columns per step"
 
+    def gate(self):
+        """The column-parallel GEMM with its fused all-gather, on a problem
+        every rank builds identically, must equal the single-GPU
+        kc_gemm_w4a16 of the full problem bit for bit."""
+        if self.world == 1:
+            return True, None
+        torch = self.torch
+        import tp
+        M, K, N = 256, 1024, 256 * self.world
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(4321)
+        x = torch.randn(M, K, device=self.dev, generator=g).bfloat16()
+        p = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=self.dev, generator=g)
+        s = (torch.rand(N, K // GROUP, device=self.dev, generator=g) * 0.018 + 0.002).half()
+        ref = torch.empty(M, N, dtype=torch.bfloat16, device=self.dev)
+        self.kc_lib.check(self.l.kc_gemm_w4a16(x.data_ptr(), p.data_ptr(), s.data_ptr(),
+                                               ref.data_ptr(), 0, M, N, K, GROUP, N, self.s_ptr))
+        col = tp.ColParallelW4A16(M, N, K, GROUP)
+        ps, ss = tp.shard_w4_rows(p, s, self.world, self.rank)
+        out = col(x, ps, ss).clone()
+        torch.cuda.synchronize()
+        col.close()
+        ok = bool(torch.equal(out, ref))
+        return ok, {"check": f"column parallel x{self.world} on [{M}, {K}] x [{N}, {K}]^T "
+                             "vs the single-GPU kc_gemm_w4a16, bit-equal",
+                    "passed": ok, "normwise_err": _normwise(out, ref)}
+
+    def close(self):
+        if self.col is not None:
+            self.col.close()
+
 
 class GemmFP8(Workload):
     name = "gemm_fp8"
+    workload_id = "fp8-w8a8-gemm-4096x8192x8192"
     metric = "FP8 W8A8 GEMM TFLOP/s (M=4096, K=8192, N=8192)"
     unit = "TFLOP/s"
     bound = "tensor-fp8"
@@ -523,7 +588,7 @@ class GemmFP8(Workload):
                 f"full rows), bf16 partials summed by {how}")
 
     def config(self):
-        return {"workload": "fp8-w8a8-gemm-4096x8192x8192", "M": self.M, "N": self.N,
+        return {"workload": self.workload_id, "M": self.M, "N": self.N,
                 "K": self.K, "scales": "per-token x per-channel", "out": "bf16",
                 "l2": f"{self.COPIES} rotating operand sets of 168 MB (larger than L2)",
                 "e2e": "fp32 activations -> kc_quantize_fp8_per_token -> kc_gemm_fp8 -> bf16"}
@@ -569,9 +634,51 @@ class GemmFP8(Workload):
         fn, flops = cls._cpu(16)
         return fn, flops, "16 of 4096 token rows x all 8192 columns per step"
 
+    def gate(self):
+        """The row-parallel GEMM and its bf16 sum, on a problem every rank
+        builds identically, must match the single-GPU kc_gemm_fp8 of the full
+        K (fp32 output) within 1e-2 normwise: each rank's partial is rounded
+        to bf16 before the sum."""
+        if self.world == 1:
+            return True, None
+        torch = self.torch
+        import tp
+        M, N, K = 256, 512, 512 * self.world
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(4322)
+        x = torch.randn(M, K, device=self.dev, generator=g)
+        x[:, torch.randperm(K, device=self.dev, generator=g)[:max(1, K // 100)]] *= 20.0
+        w = torch.randn(N, K, device=self.dev, generator=g) * 0.02
+        qa = torch.empty(M, K, dtype=torch.int8, device=self.dev)
+        qw = torch.empty(N, K, dtype=torch.int8, device=self.dev)
+        sa = torch.empty(M, dtype=torch.float32, device=self.dev)
+        sw = torch.empty(N, dtype=torch.float32, device=self.dev)
+        l, chk = self.l, self.kc_lib.check
+        chk(l.kc_quantize_fp8_per_token(x.data_ptr(), qa.data_ptr(), sa.data_ptr(), M, K, self.s_ptr))
+        chk(l.kc_quantize_fp8_per_channel(w.data_ptr(), qw.data_ptr(), sw.data_ptr(), N, K, self.s_ptr))
+        ref = torch.empty(M, N, dtype=torch.float32, device=self.dev)
+        chk(l.kc_gemm_fp8(qa.data_ptr(), sa.data_ptr(), qw.data_ptr(), sw.data_ptr(), ref.data_ptr(),
+                          1, M, N, K, N, self.s_ptr))
+        k0, k1 = tp.shard_range(K, self.world, self.rank)
+        rp = tp.RowParallelFP8(M, N, reduce=self.rp.reduce)
+        out = rp(qa[:, k0:k1].contiguous(), sa, qw[:, k0:k1].contiguous(), sw).clone()
+        torch.cuda.synchronize()
+        rp.close()
+        err = _normwise(out, ref)
+        ok = err <= 1e-2
+        return ok, {"check": f"row parallel x{self.world} ({self.rp.reduce} sum) on "
+                             f"[{M}, {K}] x [{N}, {K}]^T vs the single-GPU kc_gemm_fp8, "
+                             "normwise <= 1e-2",
+                    "passed": ok, "normwise_err": err}
+
+    def close(self):
+        if self.rp is not None:
+            self.rp.close()
+
 
 class QuantFP8(Workload):
     name = "quant_fp8"
+    workload_id = "fp8-per-token-quant-8192x8192"
     metric = "FP8 E4M3 per-token quantization GB/s (T=8192, D=8192)"
     dtype = "f32->e4m3"
     data = "synthetic (x N(0,1) with 1% of channels, fixed by seed, scaled x20)"
@@ -599,7 +706,7 @@ class QuantFP8(Workload):
         return self.T * self.D * 4 + self.T * self.D + self.T * 4
 
     def config(self):
-        return {"workload": "fp8-per-token-quant-8192x8192", "T": self.T, "D": self.D,
+        return {"workload": self.workload_id, "T": self.T, "D": self.D,
                 "bytes_per_step": self.work_per_step(),
                 "l2": "input 268 MB (larger than L2)"}
 
@@ -636,6 +743,7 @@ class QuantFP8(Workload):
 
 class GemvInt4(Workload):
     name = "gemv_int4"
+    workload_id = "int4-gemv-ref-abi-4096x4096"
     metric = "INT4 dequant+GEMV HBM GB/s (reference ABI, fp32, 4096x4096)"
     dtype = "f32"
     data = ("synthetic (uniform nibbles, packed^0x88 with zero points 0, fp32 scales "
@@ -674,7 +782,7 @@ class GemvInt4(Workload):
         return R * C // 2 + R * (C // GROUP) * 4 + R * (C // GROUP // 2) + C * 4 + R * 4
 
     def config(self):
-        return {"workload": "int4-gemv-ref-abi-4096x4096", "rows": self.R, "cols": self.C,
+        return {"workload": self.workload_id, "rows": self.R, "cols": self.C,
                 "group_size": GROUP, "bytes_per_step": self.work_per_step(),
                 "l2": f"{self.COPIES} rotating weight copies = 288 MB (larger than L2)"}
 
@@ -714,6 +822,7 @@ class GemvInt4(Workload):
 
 class MlpW4A16(Workload):
     name = "mlp_w4a16"
+    workload_id = "w4a16-mlp-block-2048x4096x16384"
     metric = "W4A16 MLP block TFLOP/s (M=2048, H=4096, I=16384, GELU, group 128)"
     unit = "TFLOP/s"
     bound = "tensor-bf16"
@@ -763,7 +872,7 @@ class MlpW4A16(Workload):
                 "no communication between the GEMMs, one NCCL fp32 all-reduce per step")
 
     def config(self):
-        return {"workload": "w4a16-mlp-block-2048x4096x16384", "M": self.M, "H": self.H,
+        return {"workload": self.workload_id, "M": self.M, "H": self.H,
                 "I": self.I, "group_size": GROUP, "activation": "gelu_quick (x*sigmoid(1.702x))",
                 "out": "fp32",
                 "l2": f"{self.COPIES} rotating weight sets of 66 MB each, and the 64 MB bf16 "
@@ -803,6 +912,28 @@ class MlpW4A16(Workload):
 
 
 WORKLOADS = {w.name: w for w in (GemvW4A16, GemmW4A16, GemmFP8, QuantFP8, GemvInt4, MlpW4A16)}
+# the default run: one line each, the headline decode GEMV last
+DEFAULT_SET = ("gemv_int4", "quant_fp8", "gemm_w4a16", "gemm_fp8", "gemv")
+
+
+def _selected(args) -> list:
+    return list(DEFAULT_SET) if args.workload == "all" else [args.workload]
+
+
+def _spread(ms: list) -> dict:
+    """Median and 10th / 90th percentiles of per-step device times (ms)."""
+    a = np.asarray(ms, np.float64)
+    return {"median": round(float(np.median(a)), 4), "p10": round(float(np.percentile(a, 10)), 4),
+            "p90": round(float(np.percentile(a, 90)), 4), "n": int(a.size)}
+
+
+def fp8_peak() -> dict | None:
+    """The dense FP8 tensor-core figure measured on this pool's B200s with
+    torch._scaled_mm (profiles/fp8_peak.json, written by a builder run)."""
+    p = ROOT / "profiles" / "fp8_peak.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return None
 
 
 # --------------------------------------------------------------------------
@@ -811,75 +942,50 @@ WORKLOADS = {w.name: w for w in (GemvW4A16, GemmW4A16, GemmFP8, QuantFP8, GemvIn
 def run_reference(args) -> None:
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    W = WORKLOADS[args.workload]
-    fn, work, sample = W.reference_step()
-    for _ in range(args.warmup):
-        fn()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        fn()
-    dt = (time.perf_counter() - t0) / args.steps
-    scale = 1e-9 if W.unit == "GB/s" else 1e-12
-    val = work / dt * scale
-    cores = os.cpu_count() or 1
-    line = {
-        "impl": "reference", "metric": W.metric, "value": round(val, 5), "unit": W.unit,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "CPU port (f64 accumulation where the path reduces)",
-        "data": "synthetic",
-        "config": {"workload": W.name, "sample": sample},
-        "cpu_baseline": {"value": round(val, 5), "unit": W.unit, "cores": cores, "kind": "port",
-                         "sample": sample},
-        "e2e": {"value": round(val, 5), "unit": W.unit, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+    for name in _selected(args):
+        W = WORKLOADS[name]
+        fn, work, sample = W.reference_step()
+        for _ in range(args.warmup):
+            fn()
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            fn()
+            times.append((time.perf_counter() - t0) * 1e3)
+        dt = sum(times) / len(times) / 1e3
+        scale = 1e-9 if W.unit == "GB/s" else 1e-12
+        val = work / dt * scale
+        cores = os.cpu_count() or 1
+        line = {
+            "impl": "reference", "metric": W.metric, "value": round(val, 5), "unit": W.unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 3), "step_ms": _spread(times), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "CPU port (f64 accumulation where the path reduces)", "data": "synthetic",
+            "config": {"workload": W.workload_id, "sample": sample},
+            "cpu_baseline": {"value": round(val, 5), "unit": W.unit, "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(val, 5), "unit": W.unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
 
 
 # --------------------------------------------------------------------------
 # kc arm
 # --------------------------------------------------------------------------
-def main(argv=None) -> int:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="kc", choices=["kc", "reference"])
-    ap.add_argument("--workload", default="gemv", choices=sorted(WORKLOADS))
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e pass")
-    ap.add_argument("--no-graph", action="store_true",
-                    help="gemv: launch the step eagerly instead of replaying it as a CUDA graph")
-    ap.add_argument("--layers", type=int, default=LAYERS,
-                    help="gemv: decoder layers per step (default 32; fewer only for profiling)")
-    ap.add_argument("--heat-s", type=float, default=1.5,
-                    help="seconds of the same workload run right before the timed region "
-                         "(the clock sampler covers it and the timed region)")
-    args = ap.parse_args(argv)
-    args.warmup = max(args.warmup, 3)
+def _max_over_ranks(torch, dist, world, dev, vals):
+    if world == 1:
+        return list(vals)
+    t = torch.tensor(list(vals), device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
 
-    if args.impl == "reference":
-        run_reference(args)
-        return 0
 
-    import torch
-    import torch.distributed as dist
-    from kc_lib import lib
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", torch.cuda.current_device())
-    l = lib()
-    stream = torch.cuda.current_stream()
-    s_ptr = ctypes.c_void_p(stream.cuda_stream)
-
-    W = WORKLOADS[args.workload]
+def run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, local) -> int:
+    """One workload: gate (N > 1), warm-up, heat, K timed steps, e2e, one
+    JSON line from rank 0.  Returns the exit status (3: the gate failed)."""
+    W = WORKLOADS[name]
     if W is GemvW4A16:
         wl = W(torch, l, dev, s_ptr, rank, world, layers=args.layers)
         wl.use_graph = not args.no_graph
@@ -887,17 +993,32 @@ def main(argv=None) -> int:
         wl = W(torch, l, dev, s_ptr, rank, world)
     torch.cuda.synchronize()
 
-    t_w = time.perf_counter()
+    ok, gate = wl.gate()
+    if world > 1:
+        t = torch.tensor([1.0 if ok else 0.0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok = bool(t.item() == 1.0)
+    if not ok:
+        if rank == 0:
+            print(json.dumps({"metric": wl.metric, "error": "multi-GPU correctness gate failed",
+                              "gate": gate, "n_gpus": world}), flush=True)
+        wl.close()
+        return 3
+
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
-    # heat phase: a step COUNT every rank agrees on (steps may contain
-    # collectives, so all ranks must run the same number of them)
-    per_step = (time.perf_counter() - t_w) / args.warmup
-    if world > 1:
-        t = torch.tensor([per_step], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        per_step = float(t.item())
+    # heat phase sized from a timing taken after the warm-up (the first
+    # warm-up steps include one-time set-up such as a graph capture); a step
+    # COUNT every rank agrees on, since steps may contain collectives
+    probe = 3
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    for _ in range(probe):
+        wl.step()
+    p1.record(stream)
+    torch.cuda.synchronize()
+    per_step = _max_over_ranks(torch, dist, world, dev, [p0.elapsed_time(p1) / probe / 1e3])[0]
     heat_steps = int(min(args.heat_s / max(per_step, 1e-6), 20000))
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -909,24 +1030,24 @@ def main(argv=None) -> int:
             torch.cuda.synchronize()
     torch.cuda.synchronize()
 
-    # ---- timed region ------------------------------------------------------
+    # ---- timed region: exactly K steps, an event between steps ---------------
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    evs[0].record(stream)
+    for i in range(args.steps):
         wl.step()
-    e1.record(stream)
+        evs[i + 1].record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    ms = evs[0].elapsed_time(evs[-1])
+    # max over ranks: the whole region, and each step's time
+    both = _max_over_ranks(torch, dist, world, dev, [ms] + step_ms)
+    ms, step_ms = both[0], both[1:]
     ms_step = ms / args.steps
     work = wl.work_per_step()
     sc = wl.scale()
@@ -949,11 +1070,7 @@ def main(argv=None) -> int:
             stream.synchronize()
         e3.record(stream)
         torch.cuda.synchronize()
-        ms_e2e = e2.elapsed_time(e3)
-        if world > 1:
-            t = torch.tensor([ms_e2e], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms_e2e = float(t.item())
+        ms_e2e = _max_over_ranks(torch, dist, world, dev, [e2.elapsed_time(e3)])[0]
         e2e = {"value": round(world * work / (ms_e2e / args.steps * 1e-3) * sc, 3),
                "unit": wl.unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
@@ -966,8 +1083,15 @@ def main(argv=None) -> int:
         peak, unit, bound = peaks["bf16_tflops_sustained"], "TFLOP/s", "tensor"
         psrc = peaks["source"] + " (cuBLAS bf16, sustained under the power cap)"
     else:
-        peak, unit, bound = 2 * peaks["bf16_tflops_sustained"], "TFLOP/s", "tensor"
-        psrc = peaks["source"] + " (2 x cuBLAS bf16 sustained; no measured fp8 peak)"
+        f8 = fp8_peak()
+        unit, bound = "TFLOP/s", "tensor"
+        if f8 is not None:
+            peak = f8["fp8_tflops_sustained"]
+            psrc = ("builder-measured dense FP8: torch._scaled_mm e4m3, sustained under the power "
+                    "cap (profiles/fp8_peak.json)")
+        else:
+            peak = 2 * peaks["bf16_tflops_sustained"]
+            psrc = peaks["source"] + " (2 x cuBLAS bf16 sustained; no measured fp8 peak)"
     traffic = profile_traffic(wl.profile)
 
     cpu = None
@@ -977,9 +1101,12 @@ def main(argv=None) -> int:
     if rank == 0:
         cfg = wl.config()
         cfg["parallelism"] = wl.parallelism()
+        if gate is not None:
+            cfg["gate"] = gate
         line = {
             "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "step_ms": _spread(step_ms),
             "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
             "data": wl.data, "config": cfg,
             "roofline": {"bound": bound, "achieved": round(per_gpu, 1), "peak": peak,
@@ -993,10 +1120,122 @@ def main(argv=None) -> int:
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    wl.close()
+    del wl
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return 0
+
+
+def measure_peak(kind: str, seconds: float, reps: int) -> dict:
+    """Dense tensor-core throughput of the library GEMM this pool's roofline
+    denominators come from: torch.matmul bf16 8192^3 ("bf16") or
+    torch._scaled_mm e4m3 x e4m3 -> bf16 8192^3 with unit scales ("fp8");
+    best of `reps` CUDA-event timed launches (burst) and the mean over
+    `seconds` of back-to-back launches (sustained, under the power cap)."""
+    import torch
+    n = 8192
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    a = torch.randn(n, n, device=dev, generator=g)
+    b = torch.randn(n, n, device=dev, generator=g)
+    if kind == "bf16":
+        a, b = a.bfloat16(), b.bfloat16()
+        fn = lambda: torch.matmul(a, b)  # noqa: E731
+    else:
+        a8 = a.to(torch.float8_e4m3fn)
+        b8 = b.to(torch.float8_e4m3fn).t()     # column-major second operand
+        one = torch.ones((), device=dev)
+        fn = lambda: torch._scaled_mm(a8, b8, scale_a=one, scale_b=one,  # noqa: E731
+                                      out_dtype=torch.bfloat16)
+    flops = 2.0 * n ** 3
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    sampler = ClockSampler(str(torch.cuda.current_device()))
+    sampler.start()
+    count, t0 = 0, time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    while time.perf_counter() - t0 < seconds:
+        for _ in range(8):
+            fn()
+        count += 8
+        torch.cuda.synchronize()
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    return {"kind": kind, "gemm": f"{n}^3", "how": ("torch.matmul bf16" if kind == "bf16" else
+                                                     "torch._scaled_mm e4m3 x e4m3 -> bf16"),
+            f"{kind}_tflops": round(flops / (best * 1e-3) / 1e12, 1),
+            f"{kind}_tflops_sustained": round(flops * count / (e0.elapsed_time(e1) * 1e-3) / 1e12, 1),
+            "sustained_launches": count, "clocks": clocks, "torch": torch.__version__}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--peak", choices=["bf16", "fp8"], default=None,
+                    help="measure a library GEMM's dense tensor-core peak instead (one JSON line)")
+    ap.add_argument("--peak-seconds", type=float, default=4.0)
+    ap.add_argument("--peak-reps", type=int, default=10)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="kc", choices=["kc", "reference"])
+    ap.add_argument("--workload", default="all", choices=["all"] + sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e pass")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="gemv: launch the step eagerly instead of replaying it as a CUDA graph")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="gemv: decoder layers per step (default 32; fewer only for profiling)")
+    ap.add_argument("--heat-s", type=float, default=1.5,
+                    help="seconds of the same workload run right before the timed region "
+                         "(the clock sampler covers it and the timed region)")
+    args = ap.parse_args(argv)
+    args.warmup = max(args.warmup, 3)
+
+    if args.peak is not None:
+        print(json.dumps(measure_peak(args.peak, args.peak_seconds, args.peak_reps)), flush=True)
+        return 0
+    if args.impl == "reference":
+        run_reference(args)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+    from kc_lib import lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    l = lib()
+    stream = torch.cuda.current_stream()
+    s_ptr = ctypes.c_void_p(stream.cuda_stream)
+
+    rc = 0
+    for name in _selected(args):
+        rc = run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, local)
+        if rc:
+            break
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    return 0
+    return rc
 
 
 if __name__ == "__main__":

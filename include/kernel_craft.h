@@ -146,6 +146,22 @@ KC_API void launch_verify_draft_tokens(const float* d_draft_probs, const float* 
                                 const float* d_rand_vals2, int* d_accepted, int* d_corrected,
                                 int num_tokens, int vocab_size, cudaStream_t stream);
 
+/* Further out-of-scope launchers that the reference's pybind11 module links
+ * (src/python/pybind_transformer.cpp:75,95,102,107); exported so the
+ * unmodified module loads against this library and its quantization and
+ * tensor-parallel functions work.  Each records KC_ERR_UNSUPPORTED and
+ * launches nothing. */
+KC_API void launch_compute_prefix_length(const int* d_accepted, int* d_prefix_len, int num_tokens,
+                                         cudaStream_t stream);
+KC_API void launch_selective_scan(const float* d_u, const float* d_A_log, const float* d_B,
+                                  const float* d_C, const float* d_delta, float* d_y,
+                                  int B_, int L, int D, int N_state, cudaStream_t stream);
+KC_API void launch_depthwise_conv1d(const float* d_x, const float* d_w, const float* d_bias,
+                                    float* d_y, int B_, int D, int L, int d_conv,
+                                    cudaStream_t stream);
+KC_API void launch_rmsnorm(const float* d_x, const float* d_g, float* d_y, int rows, int D,
+                           float eps, cudaStream_t stream);
+
 /* ======================================================================= */
 /* Part 2: kc_* API                                                          */
 /* ======================================================================= */
@@ -216,11 +232,15 @@ KC_API int kc_quantize_fp8_per_tensor_dynamic(const float* in, int8_t* out, floa
  *    workspace variant above);
  *  - the first call on each device (with that device current) looks up the
  *    scratch address with cudaGetSymbolAddress; make that first call before
- *    capturing any stream;
+ *    capturing any stream.  The address is cached per device and context, so
+ *    the first call after a cudaDeviceReset, or under another context of the
+ *    same device, looks it up again (and so must precede a capture too);
  *  - one arrival counter in the scratch must read zero when a call starts: it
  *    is zero when the library loads and every completed call leaves it at zero;
- *  - calls that overlap on one device (different streams, threads or processes
- *    sharing a context) share the scratch and race; serialize them. */
+ *  - every thread and stream of one process that uses a device shares that
+ *    device's scratch, so calls that overlap on the GPU race; serialize them.
+ *    Another process loads its own copy of the library's device image and
+ *    does not share it. */
 KC_API int kc_quantize_fp8_per_tensor_dynamic_noalloc(const float* in, int8_t* out,
                                                       float* scale_out, long count,
                                                       cudaStream_t stream);
@@ -309,12 +329,23 @@ KC_API int kc_allreduce_bf16_peer(const void* const* partials, void* const* outs
 /* Stream-ordered barrier of the ranks of one node over peer memory (no
  * reference counterpart).  flags[r]: rank r's array of KC_MAX_RANKS ints
  * (zeroed once before first use; own array at index `rank`, peers' through
- * kc_ipc_open).  Every rank calls it with the same, increasing epoch (> 0);
- * one warp publishes the epoch to every rank and waits -- at most 2 s, then
- * kc_get_device_status() reports KC_ERR_TIMEOUT -- until all ranks published
- * it.  Work queued after it on the stream starts only when every rank's work
- * queued before it has finished. */
-KC_API int kc_peer_barrier(int* const* flags, int nranks, int rank, int epoch, cudaStream_t stream);
+ * kc_ipc_open).  Every rank calls it with the same, increasing epoch (> 0;
+ * compared modulo 2^32, so it may wrap); one warp publishes the epoch to
+ * every rank and waits until all ranks published it.  Work queued after it on
+ * the stream starts only when every rank's work queued before it has
+ * finished.
+ * The wait is bounded by timeout_ns (0: KC_PEER_BARRIER_DEFAULT_TIMEOUT_NS;
+ * at most KC_PEER_BARRIER_MAX_TIMEOUT_NS).  A barrier that gives up has
+ * ordered nothing: the results of the work around it are UNDEFINED.  It
+ * records KC_ERR_TIMEOUT for kc_get_device_status(), writes KC_ERR_TIMEOUT
+ * into *status_host when status_host is not NULL (pinned host memory, so the
+ * host can poll it without synchronizing), and every kc_allreduce_bf16_peer
+ * of the process writes NaN from then on, until kc_get_device_status()
+ * clears the status. */
+#define KC_PEER_BARRIER_DEFAULT_TIMEOUT_NS 2000000000ull    /* 2 s */
+#define KC_PEER_BARRIER_MAX_TIMEOUT_NS     600000000000ull  /* 10 min */
+KC_API int kc_peer_barrier(int* const* flags, int nranks, int rank, int epoch, uint64_t timeout_ns,
+                           int* status_host, cudaStream_t stream);
 
 /* fp32 C[M,N] = A[M,K] * B[N,K]^T (the column/row-parallel shard GEMM). */
 KC_API int kc_sgemm_nt(const float* A, const float* B, float* C, int M, int N, int K,

@@ -10,6 +10,7 @@
 // The per-token kernel reads each row once: a CTA holds its row in registers
 // (up to 16 float4 per thread), reduces amax across the CTA, then quantizes
 // from registers (the reference reads the row twice and stores bytes).
+#include <cuda.h>  // CUcontext (type only; the driver functions are fetched at run time)
 #include <cuda_fp8.h>
 
 #include <atomic>
@@ -288,11 +289,48 @@ __global__ void __launch_bounds__(256) amax_chunks_last_cta(const float* __restr
     }
 }
 
-// Device address of g_fp8_noalloc_scratch on the current device, looked up once
-// per device (cudaGetSymbolAddress) and cached.
+// Device address of g_fp8_noalloc_scratch in the current context, looked up
+// once per device and context (cudaGetSymbolAddress) and cached.  The cache
+// key is the context's process-unique id (cuCtxGetId), not the device
+// ordinal: after cudaDeviceReset, or under a context other than the primary
+// one, the module is loaded anew at another address, and a new id forces a
+// new lookup instead of handing out the old, dangling address.
 constexpr int kNoAllocMaxDevices = 64;
-std::atomic<unsigned int*> g_noalloc_scratch_ptr[kNoAllocMaxDevices];
+struct NoAllocSlot {
+    unsigned long long ctx_id;  // 0: not looked up yet
+    unsigned int* ptr;
+};
+NoAllocSlot g_noalloc_slot[kNoAllocMaxDevices];
 std::mutex g_noalloc_setup_mutex;
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Id of the calling thread's current context (0 when it cannot be read).
+// The driver functions are fetched through the runtime, so the library keeps
+// no link-time dependency on libcuda.
+unsigned long long current_context_id() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS ||
+        ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
 
 int noalloc_scratch(unsigned int** out) {
     int dev = 0;
@@ -300,19 +338,20 @@ int noalloc_scratch(unsigned int** out) {
     KC_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, KC_ERR_INVALID_ARG,
                "device %d beyond the %d devices the no-alloc scratch table covers", dev,
                kNoAllocMaxDevices);
-    unsigned int* p = g_noalloc_scratch_ptr[dev].load(std::memory_order_acquire);
-    if (p == nullptr) {
-        std::lock_guard<std::mutex> lock(g_noalloc_setup_mutex);
-        p = g_noalloc_scratch_ptr[dev].load(std::memory_order_relaxed);
-        if (p == nullptr) {
-            void* sym = nullptr;
-            KC_CUDA_TRY(cudaGetSymbolAddress(&sym, g_fp8_noalloc_scratch),
-                        "cudaGetSymbolAddress(no-alloc scratch)");
-            p = static_cast<unsigned int*>(sym);
-            g_noalloc_scratch_ptr[dev].store(p, std::memory_order_release);
-        }
+    std::lock_guard<std::mutex> lock(g_noalloc_setup_mutex);
+    NoAllocSlot& slot = g_noalloc_slot[dev];
+    unsigned long long id = current_context_id();  // 0 while no context is current yet
+    if (id == 0 || slot.ctx_id != id) {
+        // the lookup also makes the device's primary context current if none is
+        void* sym = nullptr;
+        KC_CUDA_TRY(cudaGetSymbolAddress(&sym, g_fp8_noalloc_scratch),
+                    "cudaGetSymbolAddress(no-alloc scratch)");
+        id = current_context_id();
+        KC_REQUIRE(id != 0, KC_ERR_CUDA, "cannot identify the current CUDA context");
+        slot.ptr = static_cast<unsigned int*>(sym);
+        slot.ctx_id = id;
     }
-    *out = p;
+    *out = slot.ptr;
     return KC_OK;
 }
 

@@ -120,21 +120,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
         if (lane == 0) {
             const uint32_t idesc = sm100::umma_idesc(sm100::kFmtE4M3, sm100::kFmtE4M3, BM, BN);
             uint32_t it = 0, t = 0;
+            bool ok = true;   // false once a wait gave up: no MMA is issued after that
             for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
                 const uint32_t acc = t & 1u;
-                sm100::mbar_wait_or_abort(&S.tmem_empty[acc], ((t >> 1) & 1u) ^ 1u, abort);
+                ok = sm100::mbar_wait_or_abort(&S.tmem_empty[acc], ((t >> 1) & 1u) ^ 1u, abort) && ok;
                 sm100::tc_fence_after();
                 const uint32_t d = tmem + acc * BN;
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
-                    sm100::mbar_wait_or_abort(&S.full[s], ph, abort);
+                    ok = sm100::mbar_wait_or_abort(&S.full[s], ph, abort) && ok;
                     sm100::tc_fence_after();
-                    const uint64_t adesc = sm100::umma_desc_sw128(sm100::smem_u32(S.a[s]));
-                    const uint64_t bdesc = sm100::umma_desc_sw128(sm100::smem_u32(S.b[s]));
+                    if (ok) {   // a stage the TMA never filled is not multiplied
+                        const uint64_t adesc = sm100::umma_desc_sw128(sm100::smem_u32(S.a[s]));
+                        const uint64_t bdesc = sm100::umma_desc_sw128(sm100::smem_u32(S.b[s]));
 #pragma unroll
-                    for (int j = 0; j < BK / 32; ++j)  // K = 32 per instruction (32 bytes)
-                        sm100::umma_f8f6f4_ss(d, adesc + 2 * j, bdesc + 2 * j, idesc,
-                                              (kb | j) != 0 ? 1u : 0u);
+                        for (int j = 0; j < BK / 32; ++j)  // K = 32 per instruction (32 bytes)
+                            sm100::umma_f8f6f4_ss(d, adesc + 2 * j, bdesc + 2 * j, idesc,
+                                                  (kb | j) != 0 ? 1u : 0u);
+                    }
+                    // committed either way, so the barriers keep completing and
+                    // every role unwinds
                     sm100::tc_commit(&S.empty[s]);  // stage free once these MMAs retire
                 }
                 sm100::tc_commit(&S.tmem_full[acc]);  // accumulator complete
@@ -152,8 +157,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
             const int m0 = (tile % P.tiles_m) * BM, n0 = (tile / P.tiles_m) * BN;
             const int m = m0 + q * 32 + lane;
             const float sam = (m < P.M) ? __ldg(P.sa + m) : 0.f;
-            sm100::mbar_wait_or_abort(&S.tmem_full[acc], (t >> 1) & 1u, abort);
+            const bool waited = sm100::mbar_wait_or_abort(&S.tmem_full[acc], (t >> 1) & 1u, abort);
             sm100::tc_fence_after();
+            // after a wait gave up anywhere in the CTA the accumulator is not a
+            // result: the tile is written as NaN, so a timeout cannot pass for
+            // plausible output (kc_get_device_status reports it as well)
+            const bool poison = !waited || *abort;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
@@ -172,6 +181,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
                     v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) * sam * s4.z;
                     v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) * sam * s4.w;
                 }
+                if (poison)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7FC00000);
                 if (P.out_f32) {
                     float* o = reinterpret_cast<float*>(P.out) + (size_t)m * P.ldc + nb;
                     if (nb + 32 <= P.N) {

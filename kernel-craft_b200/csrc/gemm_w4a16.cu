@@ -204,20 +204,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
         if (lane == 0) {
             const uint32_t idesc = sm100::umma_idesc(sm100::kFmtBF16, sm100::kFmtBF16, BW, BT);
             uint32_t it = 0, t = 0;
+            bool ok = true;   // false once a wait gave up: no MMA is issued after that
             for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
-                sm100::mbar_wait_or_abort(&S.dempty, (t & 1u) ^ 1u, abort);
+                ok = sm100::mbar_wait_or_abort(&S.dempty, (t & 1u) ^ 1u, abort) && ok;
                 sm100::tc_fence_after();
                 for (int ks = 0; ks < ksteps; ++ks, ++it) {
                     const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
-                    sm100::mbar_wait_or_abort(&S.full[s], ph, abort);
-                    sm100::mbar_wait_or_abort(&S.afull[s], ph, abort);
+                    ok = sm100::mbar_wait_or_abort(&S.full[s], ph, abort) && ok;
+                    ok = sm100::mbar_wait_or_abort(&S.afull[s], ph, abort) && ok;
                     sm100::tc_fence_after();
-                    const uint64_t bdesc = sm100::umma_desc_sw128(sm100::smem_u32(S.x[s]));
-                    const uint32_t a_tmem = tmem + kACol + s * (BK / 2);
+                    if (ok) {   // stages that were never filled are not multiplied
+                        const uint64_t bdesc = sm100::umma_desc_sw128(sm100::smem_u32(S.x[s]));
+                        const uint32_t a_tmem = tmem + kACol + s * (BK / 2);
 #pragma unroll
-                    for (int j = 0; j < BK / 16; ++j)  // K = 16 per instruction
-                        sm100::umma_f16_ts(tmem + kAccCol, a_tmem + j * 8, bdesc + 2 * j, idesc,
-                                           (ks | j) != 0 ? 1u : 0u);
+                        for (int j = 0; j < BK / 16; ++j)  // K = 16 per instruction
+                            sm100::umma_f16_ts(tmem + kAccCol, a_tmem + j * 8, bdesc + 2 * j, idesc,
+                                               (ks | j) != 0 ? 1u : 0u);
+                    }
+                    // committed either way, so the barriers keep completing
                     sm100::tc_commit(&S.empty[s]);   // activations free
                     sm100::tc_commit(&S.aempty[s]);  // TMEM A stage free
                 }
@@ -275,8 +279,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
             const int n0 = (tile / P.tiles_t) * BW, m0 = (tile % P.tiles_t) * BT;
             const int n = n0 + q * 32 + lane;
-            sm100::mbar_wait_or_abort(&S.dfull, t & 1u, abort);
+            const bool waited = sm100::mbar_wait_or_abort(&S.dfull, t & 1u, abort);
             sm100::tc_fence_after();
+            // after a wait gave up anywhere in the CTA the accumulator is not a
+            // result: the tile is written as NaN, so a timeout cannot pass for
+            // plausible output (kc_get_device_status reports it as well)
+            const float nan = __int_as_float(0x7FC00000);
+            const bool poison = !waited || *abort;
             if (P.tma_out) {
                 // the previous tile's TMA stores have finished reading the staging tile
                 if (store_lead) sm100::bulk_wait_group_read0();
@@ -298,8 +307,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
                     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + c * 64 * BW + q * 32 + lane;
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
-                        o[i * BW] = __float2bfloat16_rn(activate(__uint_as_float(r[i]), P.act));
-                        o[(32 + i) * BW] = __float2bfloat16_rn(activate(__uint_as_float(r2[i]), P.act));
+                        o[i * BW] = __float2bfloat16_rn(poison ? nan : activate(__uint_as_float(r[i]), P.act));
+                        o[(32 + i) * BW] =
+                            __float2bfloat16_rn(poison ? nan : activate(__uint_as_float(r2[i]), P.act));
                     }
                 }
                 sm100::fence_proxy_async_smem();
@@ -323,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             if (mb + i < P.M) {
-                                const float f = activate(__uint_as_float(r[i]), P.act);
+                                const float f = poison ? nan : activate(__uint_as_float(r[i]), P.act);
                                 if (P.out_f32)
                                     reinterpret_cast<float*>(P.out)[(size_t)(mb + i) * P.ldc + n] = f;
                                 else

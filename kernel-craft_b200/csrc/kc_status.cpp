@@ -70,13 +70,17 @@ int kc_get_device_status(void) {
 }
 
 // --- launchers outside this library's scope --------------------------------
-// src/python/kernel_craft_torch_ops.py:105-168 resolves these three symbols
-// when it loads libkernels.so; exporting them lets the unmodified bridge load.
+// src/python/kernel_craft_torch_ops.py:105-168 resolves the attention and
+// speculative-decoding symbols when it loads libkernels.so, and the pybind11
+// module src/python/pybind_transformer.cpp:36-122 links those plus the
+// prefix-length, Mamba and RMSNorm launchers; exporting all of them lets the
+// unmodified bridge and module load.  Each records KC_ERR_UNSUPPORTED and
+// launches nothing.
 static void kc_out_of_scope(const char* name) {
     static std::once_flag once;
     std::call_once(once, [] {
-        fprintf(stderr, "[kernel-craft-b200] attention / speculative-decoding launchers are "
-                        "not part of this library; the call launched nothing\n");
+        fprintf(stderr, "[kernel-craft-b200] attention, speculative-decoding, Mamba and RMSNorm "
+                        "launchers are not part of this library; the call launched nothing\n");
     });
     kc::set_error(KC_ERR_UNSUPPORTED, "%s is outside the quantized-linear library", name);
 }
@@ -94,6 +98,24 @@ void launch_paged_attention(const float*, const int*, const float*, const float*
 void launch_verify_draft_tokens(const float*, const float*, const int*, const float*,
                                 const float*, int*, int*, int, int, cudaStream_t) {
     kc_out_of_scope("launch_verify_draft_tokens");
+}
+
+void launch_compute_prefix_length(const int*, int*, int, cudaStream_t) {
+    kc_out_of_scope("launch_compute_prefix_length");
+}
+
+void launch_selective_scan(const float*, const float*, const float*, const float*, const float*,
+                           float*, int, int, int, int, cudaStream_t) {
+    kc_out_of_scope("launch_selective_scan");
+}
+
+void launch_depthwise_conv1d(const float*, const float*, const float*, float*, int, int, int, int,
+                             cudaStream_t) {
+    kc_out_of_scope("launch_depthwise_conv1d");
+}
+
+void launch_rmsnorm(const float*, const float*, float*, int, int, float, cudaStream_t) {
+    kc_out_of_scope("launch_rmsnorm");
 }
 
 }  // extern "C"

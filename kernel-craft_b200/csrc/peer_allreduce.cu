@@ -15,6 +15,13 @@
 // "every rank's stores are complete" after it, with kc_peer_barrier (a
 // one-warp flag exchange over the same peer mappings, bounded by a timeout)
 // or a collective on the same stream.
+//
+// A barrier that gives up has not ordered anything, so what follows it reads
+// or overwrites buffers a peer may still use.  It then records
+// KC_ERR_TIMEOUT in this unit's status word (and in the caller's host-visible
+// status slot, if one was given), and from then on every reduction of this
+// process writes NaN instead of sums, until kc_get_device_status() reads and
+// clears the word: a timeout cannot pass for a plausible result.
 #include <algorithm>
 
 #include "kc_common.cuh"
@@ -48,6 +55,7 @@ template <int R>
 __global__ void __launch_bounds__(256) peer_allreduce_bf16_kernel(const __grid_constant__ PeerPtrs p,
                                                                   long begin, long end) {
     constexpr int U = 2;
+    const bool poison = *reinterpret_cast<volatile int*>(&g_peer_status) != 0;
     const long stride = (long)gridDim.x * blockDim.x * U;
     for (long base = begin + ((long)blockIdx.x * blockDim.x + threadIdx.x) * U; base < end;
          base += stride) {
@@ -68,8 +76,9 @@ __global__ void __launch_bounds__(256) peer_allreduce_bf16_kernel(const __grid_c
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             if (base + u >= end) break;
-            const uint4 o = make_uint4(bf16x2_rn(acc[u][0], acc[u][1]), bf16x2_rn(acc[u][2], acc[u][3]),
-                                       bf16x2_rn(acc[u][4], acc[u][5]), bf16x2_rn(acc[u][6], acc[u][7]));
+            const uint4 o = poison ? make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u)
+                                   : make_uint4(bf16x2_rn(acc[u][0], acc[u][1]), bf16x2_rn(acc[u][2], acc[u][3]),
+                                                bf16x2_rn(acc[u][4], acc[u][5]), bf16x2_rn(acc[u][6], acc[u][7]));
 #pragma unroll
             for (int r = 0; r < R; ++r) __stcg(p.out[r] + base + u, o);
         }
@@ -89,9 +98,10 @@ void launch_r(const PeerPtrs& p, long begin, long end, cudaStream_t stream) {
 // this rank's own slots has reached `epoch` (acquire), at most timeout_ns.
 // Every rank launches it on its own GPU, so the wait ends as soon as the
 // slowest rank has arrived; no kernel on one GPU waits for another kernel on
-// the same GPU.
+// the same GPU.  Epochs are compared modulo 2^32 (as the difference of the
+// unsigned values read as a signed number), so they may wrap.
 __global__ void peer_barrier_kernel(const __grid_constant__ PeerPtrs p, int nranks, int rank,
-                                    int epoch, uint64_t timeout_ns) {
+                                    int epoch, uint64_t timeout_ns, int* status_slot) {
     const int lane = threadIdx.x;
     if (lane < nranks) {
         int* slot = reinterpret_cast<int*>(p.out[lane]) + rank;
@@ -103,11 +113,15 @@ __global__ void peer_barrier_kernel(const __grid_constant__ PeerPtrs p, int nran
         while (true) {
             int v;
             asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
-            if (v - epoch >= 0) break;
+            if ((int)((unsigned)v - (unsigned)epoch) >= 0) break;
             uint64_t t;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
             if (t - t0 > timeout_ns) {
                 atomicCAS(&g_peer_status, 0, KC_ERR_TIMEOUT);
+                if (status_slot != nullptr) {
+                    *reinterpret_cast<volatile int*>(status_slot) = KC_ERR_TIMEOUT;
+                    __threadfence_system();
+                }
                 break;
             }
         }
@@ -130,9 +144,28 @@ int read_device_status_peer(bool clear) {
 
 extern "C" {
 
-int kc_peer_barrier(int* const* flags, int nranks, int rank, int epoch, cudaStream_t stream) {
+int kc_peer_barrier(int* const* flags, int nranks, int rank, int epoch, uint64_t timeout_ns,
+                    int* status_host, cudaStream_t stream) {
     KC_REQUIRE(flags && nranks >= 1 && nranks <= KC_MAX_RANKS && rank >= 0 && rank < nranks,
                KC_ERR_INVALID_ARG, "rank %d of %d outside 0..%d", rank, nranks, KC_MAX_RANKS - 1);
+    KC_REQUIRE(timeout_ns <= KC_PEER_BARRIER_MAX_TIMEOUT_NS, KC_ERR_INVALID_ARG,
+               "timeout %llu ns above the maximum of %llu ns", (unsigned long long)timeout_ns,
+               (unsigned long long)KC_PEER_BARRIER_MAX_TIMEOUT_NS);
+    if (timeout_ns == 0) timeout_ns = KC_PEER_BARRIER_DEFAULT_TIMEOUT_NS;
+    int* status_dev = nullptr;
+    if (status_host != nullptr) {
+        // pinned host memory: the address the device writes through
+        KC_REQUIRE(kc::aligned(status_host, 4), KC_ERR_ALIGNMENT, "status slot not 4-byte aligned");
+        void* d = nullptr;
+        const cudaError_t e = cudaHostGetDevicePointer(&d, status_host, 0);
+        if (e != cudaSuccess) {
+            cudaGetLastError();  // not sticky: keep it from surfacing at a later launch check
+            return kc::set_error(KC_ERR_INVALID_ARG,
+                                 "status slot must be pinned, mapped host memory (%s)",
+                                 cudaGetErrorString(e));
+        }
+        status_dev = static_cast<int*>(d);
+    }
     PeerPtrs p{};
     for (int r = 0; r < nranks; ++r) {
         KC_REQUIRE(flags[r] && kc::aligned(flags[r], 4), KC_ERR_ALIGNMENT,
@@ -140,7 +173,7 @@ int kc_peer_barrier(int* const* flags, int nranks, int rank, int epoch, cudaStre
         p.in[r] = reinterpret_cast<const uint4*>(flags[r]);
         p.out[r] = reinterpret_cast<uint4*>(flags[r]);
     }
-    peer_barrier_kernel<<<1, 32, 0, stream>>>(p, nranks, rank, epoch, 2000000000ull);
+    peer_barrier_kernel<<<1, 32, 0, stream>>>(p, nranks, rank, epoch, timeout_ns, status_dev);
     return kc::check_launch("peer_barrier");
 }
 

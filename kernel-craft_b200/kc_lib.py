@@ -75,6 +75,10 @@ _PROTOS = [
     ("launch_flash_attention", None, [vp, vp, vp, vp, ci, ci, ci, ci, ci, cb, vp]),
     ("launch_paged_attention", None, [vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, vp]),
     ("launch_verify_draft_tokens", None, [vp, vp, vp, vp, vp, vp, vp, ci, ci, vp]),
+    ("launch_compute_prefix_length", None, [vp, vp, ci, vp]),
+    ("launch_selective_scan", None, [vp, vp, vp, vp, vp, vp, ci, ci, ci, ci, vp]),
+    ("launch_depthwise_conv1d", None, [vp, vp, vp, vp, ci, ci, ci, ci, vp]),
+    ("launch_rmsnorm", None, [vp, vp, vp, ci, ci, ctypes.c_float, vp]),
     # kc_* API
     ("kc_dequantize_int4_f32", ci, [vp, vp, vp, vp, ci, ci, ci, vp]),
     ("kc_gemv_int4_f32", ci, [vp, vp, vp, vp, vp, ci, ci, ci, vp]),
@@ -95,7 +99,7 @@ _PROTOS = [
     ("kc_gemm_w4a16_act", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16_allgather", ci, [vp, vp, vp, ctypes.POINTER(vp), ci, ci, ci, ci, ci, ci, vp]),
     ("kc_allreduce_bf16_peer", ci, [ctypes.POINTER(vp), ctypes.POINTER(vp), ci, ci, cl, vp]),
-    ("kc_peer_barrier", ci, [ctypes.POINTER(vp), ci, ci, ci, vp]),
+    ("kc_peer_barrier", ci, [ctypes.POINTER(vp), ci, ci, ci, ctypes.c_uint64, vp, vp]),
     ("kc_ipc_handle_bytes", ci, []),
     ("kc_ipc_alloc", ci, [ctypes.POINTER(vp), ctypes.c_size_t]),
     ("kc_ipc_free", ci, [vp]),

@@ -33,6 +33,7 @@ same functions in the same order.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import List, Tuple
 
 import torch
@@ -111,25 +112,56 @@ def check_mlp_block_w4a16(M, H, i_shard, gs, x, w1_packed, w1_scales, w2_packed,
     check_operand(w2_scales, "w2_scales", (H, i_shard // gs), _F16, cuda)
 
 
+def barrier_timeout_s() -> float:
+    """Bound of every peer-barrier wait, in seconds: $KC_PEER_BARRIER_TIMEOUT_S,
+    else 30 s -- long enough for a rank that stalls on the host between
+    steps (a checkpoint load, a first-call module load, a garbage
+    collection) to arrive late without the barrier giving up."""
+    return float(os.environ.get("KC_PEER_BARRIER_TIMEOUT_S", "30"))
+
+
 class PeerBarrier:
     """Stream-ordered barrier over peer memory (kc_peer_barrier): a one-warp
     kernel per rank exchanges an increasing epoch through flag arrays shared
-    with CUDA IPC; cheaper than a one-element NCCL collective."""
+    with CUDA IPC; cheaper than a one-element NCCL collective.
 
-    def __init__(self, group=None):
+    Each wait is bounded (``timeout_s``, default ``barrier_timeout_s()``).  A
+    wait that gives up leaves the results around it undefined; the kernel
+    then writes KC_ERR_TIMEOUT into a pinned host slot, and the next call of
+    this barrier -- or ``check()`` at a sync point -- raises ``KcError``
+    (the peer all-reduce writes NaN meanwhile)."""
+
+    def __init__(self, group=None, timeout_s: float | None = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.timeout_ns = int((barrier_timeout_s() if timeout_s is None else timeout_s) * 1e9)
         self.bufs = PeerBuffers(kc_lib.KC_MAX_RANKS * 4, group)
         self.bufs.local((kc_lib.KC_MAX_RANKS,), torch.int32).zero_()
+        # written by the device when a wait gives up; read here without a sync
+        self.status = torch.zeros(1, dtype=torch.int32).pin_memory()
         torch.cuda.synchronize()
         dist.barrier(group=group)          # every flag array is zero before first use
         self._flags = (ctypes.c_void_p * self.world)(*self.bufs.ptrs)
         self.epoch = 0
 
+    def check(self) -> None:
+        """Raise KcError if any earlier wait of this barrier gave up (only
+        waits that have already run on the device are seen: synchronize
+        first for a complete answer)."""
+        st = int(self.status[0])
+        if st != kc_lib.KC_OK:
+            raise kc_lib.KcError(st, f"a peer barrier of rank {self.rank} gave up after "
+                                     f"{self.timeout_ns / 1e9:.1f} s: the results of the calls "
+                                     "since are undefined (kc_get_device_status() clears the "
+                                     "device status)")
+
     def __call__(self) -> None:
+        self.check()
         self.epoch += 1
-        check(lib().kc_peer_barrier(self._flags, self.world, self.rank, self.epoch, _stream()))
+        check(lib().kc_peer_barrier(self._flags, self.world, self.rank, self.epoch,
+                                    self.timeout_ns, ctypes.c_void_p(self.status.data_ptr()),
+                                    _stream()))
 
     def close(self) -> None:
         torch.cuda.synchronize()

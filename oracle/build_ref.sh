@@ -4,11 +4,11 @@
 # TEST INFRASTRUCTURE ONLY: the parity tests load it as a second, independent
 # oracle on the B200.  Nothing is copied out of the reference tree.
 #
-#   KC_REF_DIR  reference checkout (default: the build machine's mount point,
-#               below); the step is skipped where no checkout exists.
+#   KC_REF_DIR  kernel-craft checkout (default: a checkout named "reference"
+#               beside this repository); the step is skipped where none exists.
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-REF="${KC_REF_DIR:-/root/reference}"
+REF="${KC_REF_DIR:-$HERE/../../reference}"
 SRC="$REF/src/kernels/transformer"
 OUT="$HERE/_ref"
 if [ ! -f "$SRC/quant_int4.cu" ]; then

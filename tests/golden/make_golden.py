@@ -29,7 +29,8 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("KC_REF_DIR", "/root/reference"))
+# the kernel-craft checkout: $KC_REF_DIR, else one named "reference" beside this repository
+REF = Path(os.environ.get("KC_REF_DIR", HERE.parent.parent.parent / "reference"))
 RAND_MAX = 2147483647
 f32 = np.float32
 

@@ -13,7 +13,9 @@ import kc_lib
 
 ROOT = Path(__file__).resolve().parent.parent
 HEADER = ROOT / "include" / "kernel_craft.h"
-REF_BRIDGE = Path(os.environ.get("KC_REF_DIR", "/root/reference")) / "src/python/kernel_craft_torch_ops.py"
+# the kernel-craft checkout: $KC_REF_DIR, else one named "reference" beside this repository
+REF_DIR = Path(os.environ.get("KC_REF_DIR", ROOT.parent / "reference"))
+REF_BRIDGE = REF_DIR / "src/python/kernel_craft_torch_ops.py"
 
 
 def declared_symbols():

@@ -255,3 +255,41 @@ def test_torch_ops_mirror(cuda):
     assert normwise_err(host(y), O.gemv_int4(packed, scales, zeros, x, rows, cols, gs)) <= GEMV_TOL
     y2 = torch.ops.kernel_craft.int4_gemv(dev(packed), dev(scales), dev(zeros), dev(x), rows, cols, gs)
     np.testing.assert_array_equal(host(y2), host(y))
+
+
+SEVEN_B = [(4096, 12288), (4096, 4096), (4096, 22016), (11008, 4096)]   # (K, N): QKV, O, gate+up, down
+
+
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_w4a16_grouped_bench_config(cuda, M):
+    """The launch bench.py times: the four 7B decode projections in ONE
+    kc_gemv_w4a16_grouped call, activations of all problems back to back in
+    one buffer and outputs in another (16-byte aligned slices), at the batch
+    sizes of the benchmark configuration; 96 seeded rows of every problem
+    (first and last row included) against the oracle, normwise <= 1e-3."""
+    gs = 128
+    kx = sum(K for K, _ in SEVEN_B)
+    ny = sum(N for _, N in SEVEN_B)
+    x_all = torch.empty(M * kx, dtype=torch.bfloat16, device=cuda)
+    y_all = torch.full((M * ny,), float("nan"), dtype=torch.float32, device=cuda)
+    keep, probs = [], []
+    xo = yo = 0
+    for i, (K, N) in enumerate(SEVEN_B):
+        packed, scales, x = _w4a16_inputs(M, N, K, gs, seed=700 + 10 * M + i)
+        dp, ds = dev(packed), dev(scales)
+        x_all[xo:xo + M * K].copy_(torch.from_numpy(x.reshape(-1).view(np.int16)).to(cuda).view(torch.bfloat16))
+        xv, yv = x_all[xo:xo + M * K], y_all[yo:yo + M * N]
+        keep.append((packed, scales, x, N, K, dp, ds, yo))
+        probs.append(kc_lib.W4A16Problem(dp.data_ptr(), ds.data_ptr(), xv.data_ptr(), yv.data_ptr(), N, K))
+        xo += M * K
+        yo += M * N
+    arr = (kc_lib.W4A16Problem * len(probs))(*probs)
+    kc_lib.check(kc_lib.lib().kc_gemv_w4a16_grouped(arr, len(probs), M, gs, stream()))
+    y_host = host(y_all)
+    assert np.all(np.isfinite(y_host))
+    for packed, scales, x, N, K, _, _, off in keep:
+        y = y_host[off:off + M * N].reshape(M, N)
+        rows = np.sort(np.random.default_rng(N + K).choice(N, 96, replace=False))
+        rows[0], rows[-1] = 0, N - 1
+        ref = O.gemv_w4a16(packed[rows], scales[rows], x, M, len(rows), K, gs)
+        assert normwise_err(y[:, rows], ref) <= GEMV_TOL, (M, K, N)

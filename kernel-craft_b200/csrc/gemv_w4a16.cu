@@ -563,6 +563,335 @@ __global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const
     }
 }
 
+// ---------------------------------------------------------------------------
+// M = 1: integer tensor-core path
+// ---------------------------------------------------------------------------
+// At batch 1 the kernel is bound by instruction issue, and most of the issue
+// went to turning nibbles into bf16 fragments (7 ALU operations per 8
+// weights).  This path feeds the weights to the integer MMA instead:
+// mma.sync m16n8k32 .u8 x .s8/.u8 runs at the same instruction rate as the
+// bf16 m16n8k16 with twice the k per instruction (measured on B200), and a
+// packed word becomes two u8 fragments with one shift and two ANDs
+// (w & 0x0F0F0F0F: k 0 2 4 6; (w >> 4) & 0x0F0F0F0F: k 1 3 5 7).
+//
+// The activations become integers once per CTA, per 128-k chunk: with f =
+// 2^-F, F chosen so max|x| * 2^F lies in [2^21, 2^22), q = rint(x * 2^F) is
+// exact for every bf16 value within 2^14 of the chunk maximum and off by at
+// most 2^-23 of that maximum otherwise.  q' = q + 2^22 in [0, 2^23) is the
+// low 23 bits of the float x * 2^F + 1.5 * 2^23 (one FMA, no conversion
+// instruction), and its three bytes B2 B1 B0 are three u8 planes.  The MMA's
+// eight columns carry the planes: column 0 = B2, 1 = B1, 2 = B0, and column
+// 3 a plane of ones, so ONE instruction per 32 k gives, per weight row,
+//   D_p = sum_k (u - 8) * B_p   (accumulator seeded with -8 * sum_k B_p)
+//   D_3 = sum_k (u - 8)         (seeded with -8 * 32 * 4 = -1024)
+// and sum_k (u - 8) * q = 65536 D_0 + 256 D_1 + D_2 - 2^22 D_3, all exact in
+// int32.  Each column is scaled by s * f in fp32 per chunk (the group scale
+// changes per chunk) and the columns are combined once per tile.
+//
+// Staged layout of one chunk (kI8ChunkBytes): for half h (k-steps 2h, 2h+1)
+// and plane p, lane t's 16 bytes [b0 b1 of step 2h | b0 b1 of step 2h+1] at
+// 192 h + 64 p + 16 t (b0: the plane's bytes of k = 32 t + 8 j + 0 2 4 6, b1:
+// of k + 1), then the record {-8 sum B_0, -8 sum B_1, -8 sum B_2, -1024, f}.
+// Lanes whose B column is 3 or more read a shared 256-byte plane of ones.
+constexpr int kI8ChunkBytes = 416;
+constexpr int kI8RecOffset = 384;
+
+struct SmemI8 {
+    using Sh = Shape<1>;
+    uint8_t ring[Sh::warps][Sh::ring][kQuad][kChunkBytes];  // TMA destinations, 1024-byte aligned
+    __half scales[Sh::groups][kScaleBufs][kScaleHalves];
+    float red[Sh::groups][2][kGroupWarps][16];   // per-warp row sums, double-buffered by tile parity
+    alignas(16) uint32_t ones[64];               // 256 bytes of 0x01
+    uint64_t wfull[Sh::warps][Sh::ring];
+    uint64_t sfull[Sh::groups][kScaleBufs];
+    int red_cnt[Sh::groups][2];
+    int red_done[Sh::groups][2];
+    // then the staged chunks: global chunk c (problem order) at c * kI8ChunkBytes
+};
+
+__host__ __device__ constexpr size_t fixed_smem_i8() { return (sizeof(SmemI8) + 127) / 128 * 128; }
+
+__device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                           uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+// Bytes `byte` of a, b, c, d (in that order) as one word.
+__device__ __forceinline__ uint32_t gather_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d,
+                                                 uint32_t byte) {
+    const uint32_t sel = byte | ((byte + 4) << 4);
+    return prmt(prmt(a, b, sel), prmt(c, d, sel), 0x5410u);
+}
+
+// Stages the one activation row (M = 1) of every problem as byte planes.
+// One thread per 8-element block; the 16 blocks of a chunk are 16
+// consecutive threads (a half warp), which reduce the chunk's maximum and
+// plane sums with shuffles.  Every thread of a warp runs the same number of
+// rounds, so the full-warp shuffles are always legal.
+__device__ __forceinline__ void stage_i8(const Params& P, uint8_t* xs) {
+    constexpr int kThreads = Shape<1>::threads;
+    const int total = P.sx_chunks * 16;  // blocks
+    const int rounds = (total + kThreads - 1) / kThreads;
+    for (int rd = 0; rd < rounds; ++rd) {
+        const int b = rd * kThreads + threadIdx.x;
+        const bool active = b < total;
+        const int c = b >> 4, r = b & 15;  // global chunk, block within the chunk
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (active) {
+            int pi = 0;
+            while (pi + 1 < P.count && c >= P.p[pi + 1].sx_off) ++pi;
+            const __nv_bfloat16* x = P.p[pi].x + (size_t)(c - P.p[pi].sx_off) * 128 + r * 8;
+            w = __ldcg(reinterpret_cast<const uint4*>(x));
+        }
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(ws[i] << 16);
+            v[2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
+        }
+        float m = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+        // NaN never wins fmaxf: a non-finite block shows up through its bits
+        bool bad = false;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bad |= (__float_as_uint(v[i]) & 0x7F800000u) == 0x7F800000u;
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) {
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            bad |= __shfl_xor_sync(0xffffffffu, (int)bad, o) != 0;
+        }
+        // m * 2^F in [2^21, 2^22): F = 148 - biased exponent of m (clamped so
+        // 2^F stays a normal float; an all-zero chunk gets F = 127 and q = 0)
+        const int e = (int)((__float_as_uint(m) >> 23) & 0xFF);
+        const int F = max(-126, min(127, 148 - e));
+        const float up = __uint_as_float((uint32_t)(127 + F) << 23);
+        const float down = bad ? __uint_as_float(0x7FC00000u) : ldexpf(1.0f, -F);
+        uint32_t q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = __float_as_uint(fmaf(v[i], up, 12582912.0f));
+        // planes: slot 0 = byte 2, slot 1 = byte 1, slot 2 = byte 0
+        uint32_t p0[3], p1[3];
+        int sum01 = 0, sum2 = 0;
+#pragma unroll
+        for (int s = 0; s < 3; ++s) {
+            p0[s] = gather_bytes(q[0], q[2], q[4], q[6], 2 - s);
+            p1[s] = gather_bytes(q[1], q[3], q[5], q[7], 2 - s);
+        }
+        // per-plane sums: plane 0 in the low 16 bits, plane 1 in the high
+        // (each at most 128 * 255 < 2^16 over the chunk), plane 2 apart
+        sum01 = __dp4a(p0[0], 0x01010101u, __dp4a(p1[0], 0x01010101u, 0u)) +
+                (int)(__dp4a(p0[1], 0x01010101u, __dp4a(p1[1], 0x01010101u, 0u)) << 16);
+        sum2 = __dp4a(p0[2], 0x01010101u, __dp4a(p1[2], 0x01010101u, 0u));
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) {
+            sum01 += __shfl_xor_sync(0xffffffffu, sum01, o);
+            sum2 += __shfl_xor_sync(0xffffffffu, sum2, o);
+        }
+        if (active) {
+            uint8_t* ch = xs + (size_t)c * kI8ChunkBytes;
+            const int t = r >> 2, j = r & 3;
+            const int off = (j >> 1) * 192 + t * 16 + (j & 1) * 8;
+#pragma unroll
+            for (int s = 0; s < 3; ++s)
+                *reinterpret_cast<uint2*>(ch + off + s * 64) = make_uint2(p0[s], p1[s]);
+            if (r == 0) {
+                *reinterpret_cast<int4*>(ch + kI8RecOffset) =
+                    make_int4(-8 * (sum01 & 0xFFFF), -8 * (int)((uint32_t)sum01 >> 16), -8 * sum2, -1024);
+                *reinterpret_cast<float*>(ch + kI8RecOffset + 16) = down;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(Shape<1>::threads, 1) gemv_w4a16_i8_kernel(const __grid_constant__ Params P) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    using Sh = Shape<1>;
+    constexpr int kGroups = Sh::groups, kWarps = Sh::warps, kRing = Sh::ring;
+    SmemI8& S = *reinterpret_cast<SmemI8*>(smem_raw);
+    uint8_t* xs = smem_raw + fixed_smem_i8();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int group = warp / kGroupWarps, gw = warp % kGroupWarps;
+    const int gtid = threadIdx.x % kGroupThreads;
+    const int g = lane >> 2, t = lane & 3;
+    const int gshift = P.gshift, total = P.total_tiles;
+    const int first = blockIdx.x + group * gridDim.x, stride = kGroups * gridDim.x;
+
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < kWarps; ++w)
+            for (int i = 0; i < kRing; ++i) sm100::mbar_init(&S.wfull[w][i], 1);
+        for (int h = 0; h < kGroups; ++h) {
+            for (int i = 0; i < kScaleBufs; ++i) sm100::mbar_init(&S.sfull[h][i], 1);
+            S.red_cnt[h][0] = S.red_cnt[h][1] = 0;
+            S.red_done[h][0] = S.red_done[h][1] = -1;
+        }
+        sm100::fence_barrier_init();
+    }
+    if (threadIdx.x < 64) S.ones[threadIdx.x] = 0x01010101u;
+    __syncthreads();
+
+    // prologue: scales and the first weight quads, before the wait on the
+    // previous grid (layer constants no kernel of this library writes)
+    if (gtid == 0)
+        for (int i = 0; i < kScaleBufs && first + i * stride < total; ++i)
+            issue_scales(P, first + i * stride, S.scales[group][i], &S.sfull[group][i]);
+    Cursor pf;
+    pf.tile = first;
+    pf.c = pf.cend = 0;
+    pf.pi = 0;
+    pf.step = stride;
+    if (pf.tile < total) {
+        pf.pi = problem_index(P, pf.tile);
+        warp_chunks(P.p[pf.pi].K >> 7, gw, pf.c, pf.cend);
+        cursor_settle(P, pf, gw);
+    }
+    const bool leader = lane == 0;
+    const uint32_t ring0 = sm100::smem_u32(&S.ring[warp][0][0][0]);
+    const uint32_t bar0 = sm100::smem_u32(&S.wfull[warp][0]);
+    for (int s = 0; s < kRing; ++s)
+        issue_quad(P, pf, ring0 + s * kQuad * kChunkBytes, bar0 + 8 * s, gw, leader);
+
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    stage_i8(P, xs);
+    __syncthreads();
+
+    // this lane's B column: planes for g < 3, the ones plane otherwise
+    const uint32_t xs_u32 = sm100::smem_u32(xs);
+    const uint32_t xlane = g < 3 ? xs_u32 + g * 64 + t * 16 : sm100::smem_u32(S.ones) + t * 16;
+    const uint32_t xstep = g < 3 ? (uint32_t)kI8ChunkBytes : 0u;
+    // the record of chunk 0: this lane's two column seeds (columns 2t, 2t + 1;
+    // lanes t >= 2 hold columns no plane feeds) and the chunk factor f
+    const uint32_t rec0 = xs_u32 + kI8RecOffset;
+    const uint32_t seed_off = t == 0 ? 0u : 8u;
+    const uint32_t ring_base = ring0 + g * 64 + 16 * t;
+    const uint32_t kMask = 0x0F0F0F0Fu;
+    uint32_t it = 0, ti = 0;
+    int pi = 0;
+    for (int tile = first; tile < total; tile += stride, ++ti) {
+        while (pi + 1 < P.count && tile >= P.p[pi + 1].tile_begin) ++pi;
+        const Prob& pr = P.p[pi];
+        const int N = pr.N, C = pr.K >> 7;
+        const int row0 = (tile - pr.tile_begin) * 16;
+        const uint32_t sb = ti % kScaleBufs;
+        sm100::mbar_wait(&S.sfull[group][sb], (ti / kScaleBufs) & 1u);
+        const int G = gshift == 31 ? 1 : (C >> gshift);
+        const uint32_t sa_base = sm100::smem_u32(&S.scales[group][sb][g * G]);
+        const uint32_t sb_base = sa_base + 16 * G;
+        const uint32_t xp = xlane + xstep * (uint32_t)pr.sx_off;          // chunk 0 of this problem
+        const uint32_t recp = rec0 + (uint32_t)(kI8ChunkBytes * pr.sx_off);
+
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        int c_begin, c_end;
+        warp_chunks(C, gw, c_begin, c_end);
+        for (int q0 = c_begin; q0 < c_end; q0 += kQuad, ++it) {
+            const uint32_t s = it % kRing, ph = (it / kRing) & 1u;
+            const int nq = min(kQuad, c_end - q0);
+            const uint32_t st = ring_base + s * (kQuad * kChunkBytes);
+            sm100::mbar_wait(&S.wfull[warp][s], ph);
+#pragma unroll
+            for (int j = 0; j < kQuad; ++j) {
+                if (j < nq) {
+                    const uint32_t c = (uint32_t)(q0 + j);
+                    const uint32_t xa = xp + c * xstep;
+                    const uint4 X0 = lds128(xa), X1 = lds128(xa + 192);
+                    const uint32_t rec = recp + c * kI8ChunkBytes;
+                    const uint2 seed = lds64(rec + seed_off);
+                    const float f = __uint_as_float(lds32(rec + 16));
+                    const uint4 WA = lds128(st + j * kChunkBytes);
+                    const uint4 WB = lds128(st + j * kChunkBytes + 512);
+                    const int grp = (int)c >> gshift;
+                    const float fa = lds_half(sa_base + 2 * grp) * f;
+                    const float fb = lds_half(sb_base + 2 * grp) * f;
+                    int d[4] = {(int)seed.x, (int)seed.y, (int)seed.x, (int)seed.y};
+                    const uint32_t wa[4] = {WA.x, WA.y, WA.z, WA.w};
+                    const uint32_t wb[4] = {WB.x, WB.y, WB.z, WB.w};
+                    const uint32_t xb[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        imma_16832(d, wa[k] & kMask, wb[k] & kMask, (wa[k] >> 4) & kMask,
+                                   (wb[k] >> 4) & kMask, xb[2 * k], xb[2 * k + 1]);
+                    acc[0] = fmaf(fa, (float)d[0], acc[0]);
+                    acc[1] = fmaf(fa, (float)d[1], acc[1]);
+                    acc[2] = fmaf(fb, (float)d[2], acc[2]);
+                    acc[3] = fmaf(fb, (float)d[3], acc[3]);
+                }
+            }
+            __syncwarp();
+            if (leader) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_quad(P, pf, ring0 + s * kQuad * kChunkBytes, bar0 + 8 * s, gw, leader);
+        }
+        // columns -> row sums: lane t = 1 holds B0 (col 2) and the ones
+        // column (col 3), lane t = 0 B2 (col 0) and B1 (col 1)
+        const float lo_g = __shfl_down_sync(0xffffffffu, fmaf(-4194304.f, acc[1], acc[0]), 1);
+        const float lo_g8 = __shfl_down_sync(0xffffffffu, fmaf(-4194304.f, acc[3], acc[2]), 1);
+        const float v_g = fmaf(65536.f, acc[0], fmaf(256.f, acc[1], lo_g));
+        const float v_g8 = fmaf(65536.f, acc[2], fmaf(256.f, acc[3], lo_g8));
+
+        // cross-warp reduction without a barrier (as in the bf16 path): each
+        // warp stores its row sums in the slot of this tile's parity, the
+        // last of the group's warps sums them, writes y and frees the slot
+        const uint32_t slot = ti & 1u;
+        if (ti >= 2 && lane == 0) {
+            volatile int* done = &S.red_done[group][slot];
+            const uint64_t t0 = sm100::globaltimer();
+            while (*done != (int)ti - 2) {
+                if (sm100::globaltimer() - t0 > KC_WAIT_TIMEOUT_NS) {
+                    sm100::record_status(KC_ERR_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __syncwarp();
+        float* red = S.red[group][slot][gw];
+        if (t == 0) {
+            red[g] = v_g;
+            red[g + 8] = v_g8;
+        }
+        __threadfence_block();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&S.red_cnt[group][slot], 1) == kGroupWarps - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence_block();
+            if (lane == 0 && tile + kScaleBufs * stride < total) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_scales(P, tile + kScaleBufs * stride, S.scales[group][sb], &S.sfull[group][sb]);
+            }
+            if (lane < 16) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < kGroupWarps; ++w) v += S.red[group][slot][w][lane];
+                if (row0 + lane < N) pr.y[row0 + lane] = v;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                S.red_cnt[group][slot] = 0;
+                __threadfence_block();
+                *reinterpret_cast<volatile int*>(&S.red_done[group][slot]) = (int)ti;
+            }
+        }
+    }
+}
+
 // CUDA-core fallback for shapes the tensor-core path cannot take (group sizes
 // other than 128 * 2^m, K % 128 != 0, unaligned pointers).  One warp per row.
 __global__ void __launch_bounds__(256) gemv_w4a16_scalar(const __grid_constant__ Params P) {
@@ -625,6 +954,26 @@ int launch_tc(const Params& P, size_t stage_bytes, cudaStream_t stream) {
 // Shared memory left for the staged activations and their chunk sums.
 constexpr size_t kSmemLimit = 227 * 1024;
 
+int launch_i8(const Params& P, size_t stage_bytes, cudaStream_t stream) {
+    const size_t smem = fixed_smem_i8() + stage_bytes;
+    KC_CUDA_TRY(cudaFuncSetAttribute(gemv_w4a16_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem),
+                "gemv_w4a16_i8 shared-memory attribute");
+    const int groups = (P.total_tiles + Shape<1>::groups - 1) / Shape<1>::groups;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)std::min(groups, kc::sm_count()));
+    cfg.blockDim = dim3(Shape<1>::threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    KC_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_w4a16_i8_kernel, P), "gemv_w4a16_i8 launch");
+    return KC_OK;
+}
+
 int launch(Params& P, cudaStream_t stream) {
     if (P.total_tiles == 0) return KC_OK;
     bool fast = true, single_group = true;
@@ -673,6 +1022,11 @@ int launch(Params& P, cudaStream_t stream) {
         q.sx_off = (int)chunks;
         xs_bytes += (long)P.M * (2L * q.K + 16);
         chunks += q.K / 128;
+    }
+    // batch 1: the integer tensor-core path when its staged byte planes fit
+    if (P.M == 1 && fixed_smem_i8() + (size_t)chunks * kI8ChunkBytes <= kSmemLimit) {
+        P.sx_chunks = (int)chunks;
+        return launch_i8(P, (size_t)chunks * kI8ChunkBytes, stream);
     }
     const size_t fixed = NT == 1 ? fixed_smem<1>() : fixed_smem<2>();
     const size_t sx_bytes = (size_t)chunks * NT * 8 * 4;

@@ -293,3 +293,48 @@ def test_w4a16_grouped_bench_config(cuda, M):
         rows[0], rows[-1] = 0, N - 1
         ref = O.gemv_w4a16(packed[rows], scales[rows], x, M, len(rows), K, gs)
         assert normwise_err(y[:, rows], ref) <= GEMV_TOL, (M, K, N)
+
+
+def _adversarial_x(kind, K, seed):
+    """bf16 activation rows (bit patterns) that stress the batch-1 path, which
+    turns each 128-k chunk of x into integers scaled by the chunk maximum."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((1, K)).astype(np.float32)
+    if kind == "outliers":          # 1 % of channels x1000 (heavier than config 1's x20)
+        x[0, rng.permutation(K)[:max(1, K // 100)]] *= 1000.0
+    elif kind == "zero_chunks":     # whole chunks of zeros, and one all-zero row start
+        x[0, :128] = 0.0
+        x[0, 384:640] = 0.0
+    elif kind == "tiny":
+        x *= 1e-30
+    elif kind == "huge":
+        x *= 1e30
+    elif kind == "mixed":           # 1e4 and 1e-4 side by side in every chunk
+        x[0, ::2] *= 1e4
+        x[0, 1::2] *= 1e-4
+    return O.f32_to_bf16_bits(x)
+
+
+@pytest.mark.parametrize("kind", ["outliers", "zero_chunks", "tiny", "huge", "mixed"])
+def test_w4a16_batch1_activation_ranges(cuda, kind):
+    """Batch 1 against the oracle (fp64-exact products of the given bf16 values)
+    for activation distributions far from N(0, 1); normwise <= 1e-3, and
+    elementwise within 1e-3 of max |y| as well."""
+    gs, N, K = 128, 512, 4096
+    packed, scales = O.make_w4_gptq(N, K, gs, seed=41)
+    x = _adversarial_x(kind, K, seed=42)
+    y = _run_w4a16(packed, scales, x, 1, N, K, gs)
+    ref = O.gemv_w4a16(packed, scales, x, 1, N, K, gs)
+    assert np.all(np.isfinite(y))
+    if np.max(np.abs(ref)) == 0:
+        assert np.max(np.abs(y)) == 0
+    else:
+        assert normwise_err(y, ref) <= GEMV_TOL, kind
+
+
+def test_w4a16_batch1_all_zero_row(cuda):
+    gs, N, K = 128, 64, 1024
+    packed, scales = O.make_w4_gptq(N, K, gs, seed=43)
+    x = np.zeros((1, K), np.uint16)
+    y = _run_w4a16(packed, scales, x, 1, N, K, gs)
+    assert np.all(y == 0)

@@ -333,17 +333,60 @@ class GemvW4A16(Workload):
                 "l2": f"inputs larger than L2: {self.n_layers} distinct layers = "
                       f"{self.work_per_step() / 1e9:.2f} GB per step"}
 
+    E2E_PARTS = 4   # layer groups whose copies overlap the other groups' launches
+
     def e2e_prepare(self):
+        """Host buffers for the end-to-end step, and the step split into
+        E2E_PARTS groups of layers, each captured as its own CUDA graph: the
+        activations of group i+1 are copied in, and the outputs of group i-1
+        copied out, on a copy stream while group i computes."""
+        torch = self.torch
         self.h_x = self.x_all.cpu().pin_memory()
-        self.h_y = self.torch.empty(self.y_all.shape, dtype=self.y_all.dtype).pin_memory()
+        self.h_y = torch.empty(self.y_all.shape, dtype=self.y_all.dtype).pin_memory()
+        kx = sum(K for _, K, _ in SHAPES)
+        ny = sum(N for _, _, N in SHAPES)
+        per = (self.n_layers + self.E2E_PARTS - 1) // self.E2E_PARTS
+        self.parts = []
+        for p0 in range(0, self.n_layers, per):
+            p1 = min(self.n_layers, p0 + per)
+            self.parts.append((slice(p0 * kx, p1 * kx), slice(p0 * ny, p1 * ny), self.layers[p0:p1]))
+        self.copy_stream = torch.cuda.Stream()
+        st = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+        self.part_graphs = []
+        for _, _, layers in self.parts:
+            for _, arr in layers:    # one eager pass sets the kernel attributes
+                self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, st()))
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                for _, arr in layers:
+                    self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, st()))
+            self.part_graphs.append(g)
+        torch.cuda.synchronize()
         return (self.h_x.numel() * self.h_x.element_size(),
                 self.h_y.numel() * self.h_y.element_size())
 
     def e2e_step(self):
-        # every layer's activations in, the 32 grouped launches, every output out
-        self.x_all.copy_(self.h_x, non_blocking=True)
-        self.step()
-        self.h_y.copy_(self.y_all, non_blocking=True)
+        """Every layer's activations in from pinned host memory, the 32
+        grouped launches, every output out -- the copies of one layer group
+        overlapped with the launches of the others."""
+        torch = self.torch
+        main, cs = torch.cuda.current_stream(), self.copy_stream
+        ev_in = [torch.cuda.Event() for _ in self.parts]
+        ev_out = [torch.cuda.Event() for _ in self.parts]
+        cs.wait_stream(main)            # the previous step's reads of x are done
+        with torch.cuda.stream(cs):
+            for i, (xs, _, _) in enumerate(self.parts):
+                self.x_all[xs].copy_(self.h_x[xs], non_blocking=True)
+                ev_in[i].record(cs)
+        for i, (_, ys, _) in enumerate(self.parts):
+            main.wait_event(ev_in[i])
+            self.part_graphs[i].replay()
+            ev_out[i].record(main)
+            with torch.cuda.stream(cs):
+                cs.wait_event(ev_out[i])
+                self.h_y[ys].copy_(self.y_all[ys], non_blocking=True)
+        main.wait_stream(cs)            # the step ends when its last output is on the host
 
     @staticmethod
     def cpu_sample():

@@ -182,6 +182,12 @@ KC_API int kc_gemv_int4_f32(const uint8_t* packed, const float* scales, const ui
 KC_API int kc_dequantize_w4_bf16(const uint8_t* packed, const uint16_t* scales_f16, uint16_t* out_bf16,
                           int N, int K, int group_size, cudaStream_t stream);
 
+/* kc_dequantize_w4_bf16 with per-group zero points: out = bf16((u - z) * s),
+ * zeros u8[N, K/gs] (0..15); no reference counterpart (see kc_gemv_w4a16_zp). */
+KC_API int kc_dequantize_w4_bf16_zp(const uint8_t* packed, const uint16_t* scales_f16,
+                                    const uint8_t* zeros, uint16_t* out_bf16, int N, int K,
+                                    int group_size, cudaStream_t stream);
+
 /* W4A16 GEMV / skinny GEMM: y[m,n] = sum_k w[n,k] * x[m,k] for m < M <= 16;
  * x bf16[M,K], y f32[M,N], fp32 accumulation.  Fast path: group_size % 128 == 0,
  * K % 128 == 0, packed/x 16-byte aligned; other shapes take a CUDA-core path. */
@@ -203,6 +209,21 @@ typedef struct kc_w4a16_problem {
 #define KC_W4A16_MAX_PROBLEMS 8
 KC_API int kc_gemv_w4a16_grouped(const kc_w4a16_problem* problems, int count, int M,
                           int group_size, cudaStream_t stream);
+
+/* W4 with per-group zero points (AWQ and asymmetric GPTQ checkpoints):
+ * w[n,k] = (u - z[n, k/gs]) * float(scales_f16[n, k/gs]) with zeros u8[N, K/gs],
+ * one zero point (0..15) per row and group, unpacked.  z = 8 everywhere is
+ * the symmetric case above; the reference's dequantize_int4 represents only
+ * z >= 8 (its weight nibbles are signed, quant_int4.cu:34-38, and its zero
+ * points unsigned, :93-96), so these entry points have no reference twin.
+ * Batch 1 runs on the integer tensor-core path like the symmetric GEMV;
+ * M > 1 on the CUDA-core path.  Same shape rules as kc_gemv_w4a16. */
+KC_API int kc_gemv_w4a16_zp(const uint8_t* packed, const uint16_t* scales_f16, const uint8_t* zeros,
+                            const uint16_t* x_bf16, float* y, int M, int N, int K, int group_size,
+                            cudaStream_t stream);
+/* Grouped form: zeros[i] belongs to problems[i] (NULL: that problem is symmetric). */
+KC_API int kc_gemv_w4a16_grouped_zp(const kc_w4a16_problem* problems, const uint8_t* const* zeros,
+                                    int count, int M, int group_size, cudaStream_t stream);
 
 /* FP8 E4M3 per-token quantization (fp8_quant.cu:89-131 semantics, bit-exact):
  * scales[r] = amax_r > 0 ? amax_r/448 : 1; q = e4m3_satfinite(clamp(x/scale)). */
@@ -293,6 +314,15 @@ KC_API int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const ui
 KC_API int kc_gemm_w4a16_act(const uint16_t* x_bf16, const uint8_t* packed,
                              const uint16_t* scales_f16, void* out, int out_f32, int M, int N,
                              int K, int group_size, int ldc, int act, cudaStream_t stream);
+
+/* kc_gemm_w4a16_act with per-group zero points (AWQ, asymmetric GPTQ; no
+ * reference counterpart, see kc_gemv_w4a16_zp): the weights are the exact
+ * bf16((u - z[n, k/gs]) * s[n, k/gs]) that kc_dequantize_w4_bf16_zp produces,
+ * zeros u8[N, K/gs] (0..15).  Same requirements as kc_gemm_w4a16. */
+KC_API int kc_gemm_w4a16_zp(const uint16_t* x_bf16, const uint8_t* packed,
+                            const uint16_t* scales_f16, const uint8_t* zeros, void* out,
+                            int out_f32, int M, int N, int K, int group_size, int ldc, int act,
+                            cudaStream_t stream);
 
 /* Column-parallel W4A16 GEMM fused with the all-gather of its output (one
  * process per GPU; no counterpart kernel in the reference, whose

@@ -23,8 +23,10 @@ These are the layouts vLLM 0.22.0 packs and unpacks
 pack_cols, awq_pack; awq_triton.py's reverse order), which the tests use as
 the independent packer.
 
-The W4A16 kernels compute (u - 8) * s, so only symmetric checkpoints (every
-zero point 8) convert; others raise ValueError.  Act-order checkpoints convert
+Symmetric checkpoints (every zero point 8) convert to packed weights and
+scales alone, for the kernels' (u - 8) * s.  Others (AWQ usually,
+asymmetric GPTQ) convert with their zero points as well, u8 [N, K/gs] one
+per byte, for the kc_*_zp entry points ((u - z) * s).  Act-order checkpoints convert
 with a permutation of the input channels that makes every group contiguous:
 the kernels then take x[:, perm] instead of x (a gather, or folded into the
 producer of x).
@@ -42,6 +44,7 @@ class W4A16Weights(NamedTuple):
     packed: np.ndarray             # u8 [N, K/2], low nibble = even k
     scales: np.ndarray             # fp16 [N, K/gs]
     perm: Optional[np.ndarray]     # int64 [K]: the kernels take x[:, perm]; None = identity
+    zeros: Optional[np.ndarray] = None   # u8 [N, K/gs] zero points 0..15; None = all 8
 
 
 def _np(a) -> np.ndarray:
@@ -77,11 +80,12 @@ def _pack_w4(u_kn: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(u[:, 0::2] | (u[:, 1::2] << 4)).astype(np.uint8)
 
 
-def _check_symmetric(z: np.ndarray, what: str) -> None:
-    if not np.all(z == 8):
-        bad = int(np.count_nonzero(z != 8))
-        raise ValueError(f"{what}: {bad} zero points differ from 8; the W4A16 kernels compute "
-                         "(u - 8) * s and take symmetric checkpoints only")
+def _zero_points(z_gn: np.ndarray) -> Optional[np.ndarray]:
+    """Zero points [K/gs, N] -> None when every one is 8 (the symmetric kernels
+    need none), else u8 [N, K/gs] for the zero-point entry points."""
+    if np.all(z_gn == 8):
+        return None
+    return np.ascontiguousarray(z_gn.T).astype(np.uint8)
 
 
 def _group_order(g_idx: np.ndarray, K: int, group_size: int) -> Optional[np.ndarray]:
@@ -114,11 +118,13 @@ def from_gptq(qweight, qzeros, scales, g_idx=None, group_size: int = 128,
     z = _nibbles_cols(qz)[:, :N].astype(np.int32)          # [K/gs, N]
     if checkpoint_format == "gptq":
         z = (z + 1) & 0xF
-    _check_symmetric(z, "GPTQ checkpoint")
     perm = None if g_idx is None else _group_order(g_idx, K, group_size)
     if perm is not None:
         u = u[perm]
-    return W4A16Weights(_pack_w4(u), np.ascontiguousarray(s.T).astype(np.float16), perm)
+    # after the permutation, block g of the channels is group g: zero points
+    # and scales stay indexed by group
+    return W4A16Weights(_pack_w4(u), np.ascontiguousarray(s.T).astype(np.float16), perm,
+                        _zero_points(z))
 
 
 def from_awq(qweight, qzeros, scales, group_size: int = 128) -> W4A16Weights:
@@ -130,8 +136,8 @@ def from_awq(qweight, qzeros, scales, group_size: int = 128) -> W4A16Weights:
     if K % group_size or s.shape != (K // group_size, N):
         raise ValueError(f"scales {s.shape} do not match K={K}, N={N}, group_size={group_size}")
     z = _nibbles_cols(qz, _AWQ_SHIFT_OF_COL)[:, :N]
-    _check_symmetric(z, "AWQ checkpoint")
-    return W4A16Weights(_pack_w4(u), np.ascontiguousarray(s.T).astype(np.float16), None)
+    return W4A16Weights(_pack_w4(u), np.ascontiguousarray(s.T).astype(np.float16), None,
+                        _zero_points(z))
 
 
 def to_reference_abi(w: W4A16Weights, group_size: int = 128) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
@@ -142,8 +148,32 @@ def to_reference_abi(w: W4A16Weights, group_size: int = 128) -> Tuple[np.ndarray
     floor(K/gs/2) bytes (quant_int4.cu:93; its tests allocate the ceiling,
     test_quant_int4.cpp:56, which only differs for an odd group count, where
     all-zero points read the same either way).  One trailing byte keeps the
-    last row's odd group inside the buffer."""
+    last row's odd group inside the buffer.
+
+    Zero points z other than 8 become the reference's zp = z - 8 (its weight
+    (sx4(u ^ 8) - zp) * s = (u - z) * s); the reference reads zero points
+    unsigned, so z < 8 cannot be represented and raises ValueError."""
     packed = np.ascontiguousarray(w.packed ^ np.uint8(0x88))
     N, G = w.scales.shape
     zeros = np.zeros(N * (G // 2) + 1, np.uint8)
+    if w.zeros is not None:
+        z = w.zeros.astype(np.int32)
+        if np.any(z < 8):
+            raise ValueError(f"{int(np.count_nonzero(z < 8))} zero points are below 8: the reference "
+                             "ABI reads zero points unsigned after sign-extending the weights "
+                             "(quant_int4.cu:34-38, 93-96) and cannot represent them")
+        zp = (z - 8).astype(np.uint8)                       # [N, G]
+        stride = G // 2
+        body = zp[:, 0:2 * stride:2] | (zp[:, 1:2 * stride:2] << 4)   # [N, stride]
+        zeros[:N * stride] = body.reshape(-1)
+        if G % 2:
+            # the reference reads row r's last (even-indexed) group from the low
+            # nibble of byte r*stride + stride, which is row r+1's first byte:
+            # representable only when the two zero points agree
+            last, first_next = zp[:-1, G - 1], zp[1:, 0]
+            if np.any(last != first_next):
+                raise ValueError("odd group count: the reference's floor zero-point stride "
+                                 "(quant_int4.cu:93) makes row r's last group share a nibble with "
+                                 "row r+1's first; these zero points differ there")
+            zeros[N * stride] = zp[N - 1, G - 1]
     return packed, w.scales.astype(np.float32), zeros

@@ -60,6 +60,7 @@ struct alignas(64) Params {
     CUtensorMap omap[KC_MAX_RANKS];  // output bf16 {N_out, M} (pitch ldc), box {128, 256}, one
                                      // per destination buffer; valid if tma_out
     const __half* scales;
+    const uint8_t* zeros;   // per-group zero points u8[N, K/gs]; null: 8 (symmetric GPTQ)
     void* out;
     int M, N, K, gs, ldc, out_f32, tma_out;
     int act;       // KC_ACT_NONE or KC_ACT_GELU_QUICK, applied in the epilogue
@@ -142,6 +143,38 @@ __device__ __forceinline__ void dequant_word(uint32_t w, const GroupConst& g, ui
     const float w5 = __fmaf_rn(nib_float<0x00000F00u>(hi, magic), g.m8, g.a8);
     const float w6 = __fmaf_rn(nib_float<0x0000F000u>(hi, magic), g.m12, g.a12);
     const float w7 = __fmaf_rn(nib_float<0x000F0000u>(hi, magic), g.m16, g.a16);
+    out[0] = bf16x2_bits(w0, w1);
+    out[1] = bf16x2_bits(w2, w3);
+    out[2] = bf16x2_bits(w4, w5);
+    out[3] = bf16x2_bits(w6, w7);
+}
+
+// The same with a zero point z (0..15) per group.  With (2^(23-p) + z) * s
+// the constant of the window at bit 8 would need up to 16 + 11 bits, so the
+// nibbles use windows at bits p = 11, 15 and 19 of 2.0f instead (bit 23, the
+// exponent's lowest bit, stays clear): f = 2 + u * 2^(p-22), and
+//   fma(f, s * 2^(22-p), -(2^(23-p) + z) * s) = (u - z) * s
+// exactly, the constants having at most 13 + 11 bits (p = 11), 9 + 11 and
+// 5 + 11.  Nibbles 0-2 reach the windows by w << 11, 3-5 by w >> 1, 6-7 by
+// w >> 13.
+struct GroupConstZ {
+    float m11, a11, m15, a15, m19, a19;
+    __device__ __forceinline__ GroupConstZ(float s, float z)
+        : m11(s * 2048.0f), a11(s * -(4096.0f + z)), m15(s * 128.0f), a15(s * -(256.0f + z)),
+          m19(s * 8.0f), a19(s * -(16.0f + z)) {}
+};
+
+__device__ __forceinline__ void dequant_word_z(uint32_t w, const GroupConstZ& g, uint32_t magic2,
+                                               uint32_t* out) {
+    const uint32_t lo = w << 11, mid = w >> 1, hi = w >> 13;
+    const float w0 = __fmaf_rn(nib_float<0x00007800u>(lo, magic2), g.m11, g.a11);
+    const float w1 = __fmaf_rn(nib_float<0x00078000u>(lo, magic2), g.m15, g.a15);
+    const float w2 = __fmaf_rn(nib_float<0x00780000u>(lo, magic2), g.m19, g.a19);
+    const float w3 = __fmaf_rn(nib_float<0x00007800u>(mid, magic2), g.m11, g.a11);
+    const float w4 = __fmaf_rn(nib_float<0x00078000u>(mid, magic2), g.m15, g.a15);
+    const float w5 = __fmaf_rn(nib_float<0x00780000u>(mid, magic2), g.m19, g.a19);
+    const float w6 = __fmaf_rn(nib_float<0x00007800u>(hi, magic2), g.m11, g.a11);
+    const float w7 = __fmaf_rn(nib_float<0x00078000u>(hi, magic2), g.m15, g.a15);
     out[0] = bf16x2_bits(w0, w1);
     out[1] = bf16x2_bits(w2, w3);
     out[2] = bf16x2_bits(w4, w5);
@@ -237,14 +270,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
         const int row = q * 32 + lane;          // weight row within the tile
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         uint32_t it = 0;
+        const uint32_t magic2 = P.magic + 0x00800000u;   // 2.0f for the zero-point windows
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
             const int n0 = (tile / P.tiles_t) * BW;
             const int n = min(n0 + row, P.N - 1);
             const __half* srow = P.scales + (size_t)n * (P.K / P.gs);
+            const uint8_t* zrow = P.zeros ? P.zeros + (size_t)n * (P.K / P.gs) : nullptr;
             for (int ks = 0; ks < ksteps; ++ks, ++it) {
                 if ((it & 1u) != par) continue;
                 const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
-                const GroupConst gc(__half2float(__ldg(srow + __umulhi((uint32_t)(ks * BK), P.gs_recip))));
+                const uint32_t grp = __umulhi((uint32_t)(ks * BK), P.gs_recip);
+                const float sc = __half2float(__ldg(srow + grp));
                 sm100::mbar_wait_or_abort(&S.full[s], ph, abort);
                 const uint32_t wa = sm100::smem_u32(S.w[s]) + row * (BK / 2);
                 const uint4 p0 = lds128(wa), p1 = lds128(wa + 16);
@@ -252,8 +288,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
                 if (lane == 0) sm100::mbar_arrive(&S.empty[s]);  // packed bytes consumed
                 const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
                 uint32_t v[32];  // column c of the A stage holds k = 2c (low half), 2c + 1
+                if (zrow == nullptr) {
+                    const GroupConst gc(sc);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) dequant_word(words[i], gc, P.magic, v + 4 * i);
+                    for (int i = 0; i < 8; ++i) dequant_word(words[i], gc, P.magic, v + 4 * i);
+                } else {
+                    const GroupConstZ gz(sc, (float)(__ldg(zrow + grp) & 15));
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) dequant_word_z(words[i], gz, magic2, v + 4 * i);
+                }
                 sm100::mbar_wait_or_abort(&S.aempty[s], ph ^ 1u, abort);
                 __syncwarp();
                 sm100::tc_fence_after();
@@ -367,8 +410,9 @@ namespace {
 // of the product (bf16 through the TMA-store epilogue when tma_out), or, for a
 // single destination, fp32 / unaligned output through direct stores.
 int launch_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
-                      void* const* outs, int ndst, int col_off, int out_cols, int out_f32, int M,
-                      int N, int K, int group_size, int ldc, int act, cudaStream_t stream) {
+                      const uint8_t* zeros, void* const* outs, int ndst, int col_off, int out_cols,
+                      int out_f32, int M, int N, int K, int group_size, int ldc, int act,
+                      cudaStream_t stream) {
     KC_REQUIRE(x_bf16 && packed && scales_f16 && outs && outs[0], KC_ERR_INVALID_ARG,
                "null pointer argument");
     KC_REQUIRE(act == KC_ACT_NONE || act == KC_ACT_GELU_QUICK, KC_ERR_INVALID_ARG,
@@ -407,6 +451,7 @@ int launch_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint1
     P.ndst = ndst;
     P.col_off = col_off;
     P.scales = reinterpret_cast<const __half*>(scales_f16);
+    P.zeros = zeros;
     P.out = outs[0];
     P.M = M;
     P.N = N;
@@ -436,15 +481,24 @@ int kc_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t*
                   void* out, int out_f32, int M, int N, int K, int group_size, int ldc,
                   cudaStream_t stream) {
     void* outs[1] = {out};
-    return launch_gemm_w4a16(x_bf16, packed, scales_f16, outs, 1, 0, N, out_f32, M, N, K,
+    return launch_gemm_w4a16(x_bf16, packed, scales_f16, nullptr, outs, 1, 0, N, out_f32, M, N, K,
                              group_size, ldc, KC_ACT_NONE, stream);
+}
+
+int kc_gemm_w4a16_zp(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
+                     const uint8_t* zeros, void* out, int out_f32, int M, int N, int K,
+                     int group_size, int ldc, int act, cudaStream_t stream) {
+    KC_REQUIRE(zeros != nullptr, KC_ERR_INVALID_ARG, "null zero points");
+    void* outs[1] = {out};
+    return launch_gemm_w4a16(x_bf16, packed, scales_f16, zeros, outs, 1, 0, N, out_f32, M, N, K,
+                             group_size, ldc, act, stream);
 }
 
 int kc_gemm_w4a16_act(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
                       void* out, int out_f32, int M, int N, int K, int group_size, int ldc, int act,
                       cudaStream_t stream) {
     void* outs[1] = {out};
-    return launch_gemm_w4a16(x_bf16, packed, scales_f16, outs, 1, 0, N, out_f32, M, N, K,
+    return launch_gemm_w4a16(x_bf16, packed, scales_f16, nullptr, outs, 1, 0, N, out_f32, M, N, K,
                              group_size, ldc, act, stream);
 }
 
@@ -459,7 +513,7 @@ int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed_shard,
                N_shard, BW);
     const long cols = (long)N_shard * nranks;
     KC_REQUIRE(cols < (1L << 31), KC_ERR_INVALID_ARG, "output too wide");
-    return launch_gemm_w4a16(x_bf16, packed_shard, scales_shard, outs, nranks, rank * N_shard,
+    return launch_gemm_w4a16(x_bf16, packed_shard, scales_shard, nullptr, outs, nranks, rank * N_shard,
                              (int)cols, 0, M, N_shard, K, group_size, (int)cols, KC_ACT_NONE, stream);
 }
 

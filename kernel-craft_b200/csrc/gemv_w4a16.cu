@@ -49,6 +49,7 @@ namespace {
 struct Prob {
     const uint8_t* packed;
     const __half* scales;
+    const uint8_t* zeros;  // per-group zero points u8[N, K/gs] (0..15); null: 8 (symmetric GPTQ)
     const __nv_bfloat16* x;
     float* y;
     int N, K;
@@ -574,10 +575,11 @@ __global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const
 // packed word becomes two u8 fragments with one shift and two ANDs
 // (w & 0x0F0F0F0F: k 0 2 4 6; (w >> 4) & 0x0F0F0F0F: k 1 3 5 7).
 //
-// The activations become integers once per CTA, per 128-k chunk: with f =
-// 2^-F, F chosen so max|x| * 2^F lies in [2^21, 2^22), q = rint(x * 2^F) is
-// exact for every bf16 value within 2^14 of the chunk maximum and off by at
-// most 2^-23 of that maximum otherwise.  q' = q + 2^22 in [0, 2^23) is the
+// The activations become integers once per CTA: with f = 2^-F, F chosen per
+// activation row so that max|x| * 2^F lies in [2^21, 2^22), q = rint(x * 2^F)
+// is exact for every bf16 value within 2^14 of the row maximum and off by at
+// most 2^-23 of that maximum otherwise (the relative error this adds to y is
+// about 2^-23 * max|x| / rms(x), under 1e-4 even at max/rms = 1000).  q' = q + 2^22 in [0, 2^23) is the
 // low 23 bits of the float x * 2^F + 1.5 * 2^23 (one FMA, no conversion
 // instruction), and its three bytes B2 B1 B0 are three u8 planes.  The MMA's
 // eight columns carry the planes: column 0 = B2, 1 = B1, 2 = B0, and column
@@ -585,15 +587,16 @@ __global__ void __launch_bounds__(Shape<NT>::threads, 1) gemv_w4a16_kernel(const
 //   D_p = sum_k (u - 8) * B_p   (accumulator seeded with -8 * sum_k B_p)
 //   D_3 = sum_k (u - 8)         (seeded with -8 * 32 * 4 = -1024)
 // and sum_k (u - 8) * q = 65536 D_0 + 256 D_1 + D_2 - 2^22 D_3, all exact in
-// int32.  Each column is scaled by s * f in fp32 per chunk (the group scale
-// changes per chunk) and the columns are combined once per tile.
+// int32.  Each column is scaled by the group scale s in fp32 per chunk (s
+// changes per chunk); the columns are combined, and multiplied by f, once per
+// tile.
 //
 // Staged layout of one chunk (kI8ChunkBytes): for half h (k-steps 2h, 2h+1)
 // and plane p, lane t's 16 bytes [b0 b1 of step 2h | b0 b1 of step 2h+1] at
 // 192 h + 64 p + 16 t (b0: the plane's bytes of k = 32 t + 8 j + 0 2 4 6, b1:
-// of k + 1), then the record {-8 sum B_0, -8 sum B_1, -8 sum B_2, -1024, f}.
+// of k + 1), then the seeds {-8 sum B_0, -8 sum B_1, -8 sum B_2, -1024}.
 // Lanes whose B column is 3 or more read a shared 256-byte plane of ones.
-constexpr int kI8ChunkBytes = 416;
+constexpr int kI8ChunkBytes = 400;
 constexpr int kI8RecOffset = 384;
 
 struct SmemI8 {
@@ -602,6 +605,8 @@ struct SmemI8 {
     __half scales[Sh::groups][kScaleBufs][kScaleHalves];
     float red[Sh::groups][2][kGroupWarps][16];   // per-warp row sums, double-buffered by tile parity
     alignas(16) uint32_t ones[64];               // 256 bytes of 0x01
+    unsigned int row_max[KC_W4A16_MAX_PROBLEMS];   // max |x| per problem (float bits)
+    float row_f[KC_W4A16_MAX_PROBLEMS];            // f = 2^-F per problem
     uint64_t wfull[Sh::warps][Sh::ring];
     uint64_t sfull[Sh::groups][kScaleBufs];
     int red_cnt[Sh::groups][2];
@@ -620,10 +625,16 @@ __device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
+// As imma_16832, with the accumulator input C given apart from the output D
+// (the chunk's first k-step starts from the seeds without copying them).
+__device__ __forceinline__ void imma_16832_c(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                             uint32_t a3, uint32_t b0, uint32_t b1, uint32_t c0,
+                                             uint32_t c1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
 }
 
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
@@ -632,95 +643,198 @@ __device__ __forceinline__ uint2 lds64(uint32_t addr) {
     return v;
 }
 
-// Bytes `byte` of a, b, c, d (in that order) as one word.
-__device__ __forceinline__ uint32_t gather_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d,
-                                                 uint32_t byte) {
-    const uint32_t sel = byte | ((byte + 4) << 4);
-    return prmt(prmt(a, b, sel), prmt(c, d, sel), 0x5410u);
+// max that propagates NaN (a chunk holding a NaN must not look finite)
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
 }
 
+// Most chunks the batch-1 path stages (shared memory left after its fixed
+// part).
+constexpr int kI8MaxChunks = (int)((227 * 1024 - fixed_smem_i8()) / kI8ChunkBytes);
+
 // Stages the one activation row (M = 1) of every problem as byte planes.
-// One thread per 8-element block; the 16 blocks of a chunk are 16
-// consecutive threads (a half warp), which reduce the chunk's maximum and
-// plane sums with shuffles.  Every thread of a warp runs the same number of
-// rounds, so the full-warp shuffles are always legal.
-__device__ __forceinline__ void stage_i8(const Params& P, uint8_t* xs) {
-    constexpr int kThreads = Shape<1>::threads;
-    const int total = P.sx_chunks * 16;  // blocks
-    const int rounds = (total + kThreads - 1) / kThreads;
-    for (int rd = 0; rd < rounds; ++rd) {
-        const int b = rd * kThreads + threadIdx.x;
-        const bool active = b < total;
-        const int c = b >> 4, r = b & 15;  // global chunk, block within the chunk
-        uint4 w = make_uint4(0, 0, 0, 0);
-        if (active) {
-            int pi = 0;
-            while (pi + 1 < P.count && c >= P.p[pi + 1].sx_off) ++pi;
-            const __nv_bfloat16* x = P.p[pi].x + (size_t)(c - P.p[pi].sx_off) * 128 + r * 8;
-            w = __ldcg(reinterpret_cast<const uint4*>(x));
-        }
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-        float v[8];
+// One thread per pair of 8-element blocks (k-steps 2h and 2h + 1 of lane
+// slot t: 16 elements, whose planes are 16 contiguous bytes per plane); the 8
+// pairs of a chunk are 8 consecutive threads, which reduce the chunk's plane
+// sums with three shuffle levels.  Every load is issued before any is used,
+// so the loads cost one round trip; every thread of a warp runs the same
+// number of rounds, so the full-warp shuffles are legal.  Two passes: the
+// maximum of each problem's row (shared-memory atomicMax on the float bits,
+// which order like the values for non-negative floats and put NaN and Inf
+// above every finite value), a barrier, then the planes.
+__device__ __forceinline__ int chunk_problem(const Params& P, int c) {
+    int pi = 0;
+    while (pi + 1 < P.count && c >= P.p[pi + 1].sx_off) ++pi;
+    return pi;
+}
+
+__device__ __forceinline__ void bf16x8(const uint4& w, float* v) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            v[2 * i] = __uint_as_float(ws[i] << 16);
-            v[2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
-        }
-        float m = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
-        // NaN never wins fmaxf: a non-finite block shows up through its bits
-        bool bad = false;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) bad |= (__float_as_uint(v[i]) & 0x7F800000u) == 0x7F800000u;
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) {
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            bad |= __shfl_xor_sync(0xffffffffu, (int)bad, o) != 0;
-        }
-        // m * 2^F in [2^21, 2^22): F = 148 - biased exponent of m (clamped so
-        // 2^F stays a normal float; an all-zero chunk gets F = 127 and q = 0)
-        const int e = (int)((__float_as_uint(m) >> 23) & 0xFF);
-        const int F = max(-126, min(127, 148 - e));
-        const float up = __uint_as_float((uint32_t)(127 + F) << 23);
-        const float down = bad ? __uint_as_float(0x7FC00000u) : ldexpf(1.0f, -F);
-        uint32_t q[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) q[i] = __float_as_uint(fmaf(v[i], up, 12582912.0f));
-        // planes: slot 0 = byte 2, slot 1 = byte 1, slot 2 = byte 0
-        uint32_t p0[3], p1[3];
-        int sum01 = 0, sum2 = 0;
-#pragma unroll
-        for (int s = 0; s < 3; ++s) {
-            p0[s] = gather_bytes(q[0], q[2], q[4], q[6], 2 - s);
-            p1[s] = gather_bytes(q[1], q[3], q[5], q[7], 2 - s);
-        }
-        // per-plane sums: plane 0 in the low 16 bits, plane 1 in the high
-        // (each at most 128 * 255 < 2^16 over the chunk), plane 2 apart
-        sum01 = __dp4a(p0[0], 0x01010101u, __dp4a(p1[0], 0x01010101u, 0u)) +
-                (int)(__dp4a(p0[1], 0x01010101u, __dp4a(p1[1], 0x01010101u, 0u)) << 16);
-        sum2 = __dp4a(p0[2], 0x01010101u, __dp4a(p1[2], 0x01010101u, 0u));
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) {
-            sum01 += __shfl_xor_sync(0xffffffffu, sum01, o);
-            sum2 += __shfl_xor_sync(0xffffffffu, sum2, o);
-        }
-        if (active) {
-            uint8_t* ch = xs + (size_t)c * kI8ChunkBytes;
-            const int t = r >> 2, j = r & 3;
-            const int off = (j >> 1) * 192 + t * 16 + (j & 1) * 8;
-#pragma unroll
-            for (int s = 0; s < 3; ++s)
-                *reinterpret_cast<uint2*>(ch + off + s * 64) = make_uint2(p0[s], p1[s]);
-            if (r == 0) {
-                *reinterpret_cast<int4*>(ch + kI8RecOffset) =
-                    make_int4(-8 * (sum01 & 0xFFFF), -8 * (int)((uint32_t)sum01 >> 16), -8 * sum2, -1024);
-                *reinterpret_cast<float*>(ch + kI8RecOffset + 16) = down;
-            }
-        }
+    for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(ws[i] << 16);
+        v[2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
     }
 }
 
+// Plane words of one 8-element block q[0..7] (float bits holding q' in bits
+// 0..22): p0[sl] = bytes of the even elements, p1[sl] = of the odd ones; slot
+// 0 = byte 2, slot 1 = byte 1, slot 2 = byte 0.  Byte transpose: t = [a.b0
+// b.b0 a.b2 b.b2], u = [a.b1 b.b1 a.b3 b.b3] for the pairs (0,2) (4,6) (1,3)
+// (5,7), then one PRMT per plane word.
+__device__ __forceinline__ void planes8(const uint32_t* q, uint32_t* p0, uint32_t* p1) {
+    const uint32_t t02 = prmt(q[0], q[2], 0x6240u), t46 = prmt(q[4], q[6], 0x6240u);
+    const uint32_t u02 = prmt(q[0], q[2], 0x7351u), u46 = prmt(q[4], q[6], 0x7351u);
+    const uint32_t t13 = prmt(q[1], q[3], 0x6240u), t57 = prmt(q[5], q[7], 0x6240u);
+    const uint32_t u13 = prmt(q[1], q[3], 0x7351u), u57 = prmt(q[5], q[7], 0x7351u);
+    p0[0] = prmt(t02, t46, 0x7632u);
+    p0[1] = prmt(u02, u46, 0x5410u);
+    p0[2] = prmt(t02, t46, 0x5410u);
+    p1[0] = prmt(t13, t57, 0x7632u);
+    p1[1] = prmt(u13, u57, 0x5410u);
+    p1[2] = prmt(t13, t57, 0x5410u);
+}
+
+constexpr int kI8MaxPairRounds = (kI8MaxChunks * 8 + Shape<1>::threads - 1) / Shape<1>::threads;
+
+// With per-group zero points (ZP) the seeds depend on the weight row, so the
+// record holds the negated plane sums (and -128 for the ones column) and the
+// chunk multiplies them by each row's zero point; without, it holds the
+// seeds of zero point 8 directly.
+template <bool ZP>
+__device__ __forceinline__ void stage_i8(const Params& P, SmemI8& S, uint8_t* xs) {
+    constexpr int kSeedMul = ZP ? -1 : -8;
+    constexpr int kThreads = Shape<1>::threads;
+    const int total = P.sx_chunks * 8;  // block pairs
+    uint4 w[kI8MaxPairRounds][2];
+    // pair (c, r): lane slot t = r >> 1, half h = r & 1, blocks 4t + 2h, 4t + 2h + 1
+#pragma unroll
+    for (int rd = 0; rd < kI8MaxPairRounds; ++rd) {
+        const int b = rd * kThreads + threadIdx.x;
+        w[rd][0] = w[rd][1] = make_uint4(0, 0, 0, 0);
+        if (b < total) {
+            const int c = b >> 3, r = b & 7, pi = chunk_problem(P, c);
+            const uint4* x = reinterpret_cast<const uint4*>(P.p[pi].x + (size_t)(c - P.p[pi].sx_off) * 128) +
+                             4 * (r >> 1) + 2 * (r & 1);
+            w[rd][0] = __ldcg(x);
+            w[rd][1] = __ldcg(x + 1);
+        }
+    }
+    // pass 1: row maxima
+#pragma unroll
+    for (int rd = 0; rd < kI8MaxPairRounds; ++rd) {
+        if (rd * kThreads >= total) break;  // uniform over the CTA
+        const int b = rd * kThreads + threadIdx.x;
+        float v[16];
+        bf16x8(w[rd][0], v);
+        bf16x8(w[rd][1], v + 8);
+        float m = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) m = fmax_nan(m, fabsf(v[i]));
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (b < total && (b & 7) == 0) atomicMax(&S.row_max[chunk_problem(P, b >> 3)], __float_as_uint(m));
+    }
+    __syncthreads();
+    // pass 2: planes and seeds
+#pragma unroll
+    for (int rd = 0; rd < kI8MaxPairRounds; ++rd) {
+        if (rd * kThreads >= total) break;  // uniform over the CTA
+        const int b = rd * kThreads + threadIdx.x;
+        const bool active = b < total;
+        const int c = b >> 3, r = b & 7;
+        // max * 2^F in [2^21, 2^22): F = 148 - biased exponent of the row
+        // maximum (clamped so 2^F stays a normal float; an all-zero row gets
+        // F = 127 and q = 0)
+        const int e = active ? (int)((S.row_max[chunk_problem(P, c)] >> 23) & 0xFF) : 0;
+        const float up = __uint_as_float((uint32_t)(127 + max(-126, min(127, 148 - e))) << 23);
+        float v[16];
+        bf16x8(w[rd][0], v);
+        bf16x8(w[rd][1], v + 8);
+        uint32_t q[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) q[i] = __float_as_uint(fmaf(v[i], up, 12582912.0f));
+        uint32_t pa0[3], pa1[3], pb0[3], pb1[3];
+        planes8(q, pa0, pa1);       // block 4t + 2h     (k-step 2h)
+        planes8(q + 8, pb0, pb1);   // block 4t + 2h + 1 (k-step 2h + 1)
+        // plane sums: slot 0 in the low 16 bits, slot 1 in the high (each at
+        // most 128 * 255 < 2^16 over the chunk), slot 2 apart
+        uint32_t s0 = __dp4a(pa0[0], 0x01010101u, __dp4a(pa1[0], 0x01010101u,
+                      __dp4a(pb0[0], 0x01010101u, __dp4a(pb1[0], 0x01010101u, 0u))));
+        uint32_t s1 = __dp4a(pa0[1], 0x01010101u, __dp4a(pa1[1], 0x01010101u,
+                      __dp4a(pb0[1], 0x01010101u, __dp4a(pb1[1], 0x01010101u, 0u))));
+        uint32_t s2 = __dp4a(pa0[2], 0x01010101u, __dp4a(pa1[2], 0x01010101u,
+                      __dp4a(pb0[2], 0x01010101u, __dp4a(pb1[2], 0x01010101u, 0u))));
+        uint32_t s01 = s0 + (s1 << 16);
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) {
+            s01 += __shfl_xor_sync(0xffffffffu, s01, o);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        }
+        if (active) {
+            uint8_t* ch = xs + (size_t)c * kI8ChunkBytes + (r & 1) * 192 + (r >> 1) * 16;
+#pragma unroll
+            for (int sl = 0; sl < 3; ++sl)
+                *reinterpret_cast<uint4*>(ch + sl * 64) = make_uint4(pa0[sl], pa1[sl], pb0[sl], pb1[sl]);
+            if (r == 0)
+                *reinterpret_cast<int4*>(xs + (size_t)c * kI8ChunkBytes + kI8RecOffset) =
+                    make_int4(kSeedMul * (int)(s01 & 0xFFFFu), kSeedMul * (int)(s01 >> 16),
+                              kSeedMul * (int)s2, kSeedMul * 128);
+        }
+    }
+    // f = 2^-F per problem; an Inf or NaN in the row (exponent 255) makes it NaN
+    if (threadIdx.x < P.count) {
+        const int e = (int)((S.row_max[threadIdx.x] >> 23) & 0xFF);
+        S.row_f[threadIdx.x] =
+            e == 255 ? __uint_as_float(0x7FC00000u) : ldexpf(1.0f, -max(-126, min(127, 148 - e)));
+    }
+}
+
+// As imma_16832_c with a separate seed per accumulator element (rows g and
+// g + 8 differ when the zero point is per row).
+__device__ __forceinline__ void imma_16832_c4(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1, int c0, int c1,
+                                              int c2, int c3) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c2),
+          "r"(c3));
+}
+
+// One 128-k chunk of the batch-1 path for one lane: rows g and g + 8 of the
+// weight stage at wst (16 bytes each), this lane's B column of chunk c at xa
+// (two 16-byte halves 192 bytes apart), its two column seeds at rec; four
+// MMAs (32 k each), then the group scales of the two rows times the integer
+// sums into the fp32 column accumulators.
+// With zero points, za and zb are the zero points of rows g and g + 8.
+template <bool ZP>
+__device__ __forceinline__ void i8_chunk(uint32_t wst, uint32_t xa, uint32_t rec, uint32_t sa,
+                                         uint32_t sb, int za, int zb, float (&acc)[4]) {
+    constexpr uint32_t m = 0x0F0F0F0Fu;
+    const uint4 X0 = lds128(xa), X1 = lds128(xa + 192);
+    const uint2 seed = lds64(rec);
+    const uint4 WA = lds128(wst), WB = lds128(wst + 512);
+    const float fa = lds_half(sa), fb = lds_half(sb);
+    int d[4];
+    if (ZP)
+        imma_16832_c4(d, WA.x & m, WB.x & m, (WA.x >> 4) & m, (WB.x >> 4) & m, X0.x, X0.y,
+                      za * (int)seed.x, za * (int)seed.y, zb * (int)seed.x, zb * (int)seed.y);
+    else
+        imma_16832_c(d, WA.x & m, WB.x & m, (WA.x >> 4) & m, (WB.x >> 4) & m, X0.x, X0.y, seed.x, seed.y);
+    imma_16832(d, WA.y & m, WB.y & m, (WA.y >> 4) & m, (WB.y >> 4) & m, X0.z, X0.w);
+    imma_16832(d, WA.z & m, WB.z & m, (WA.z >> 4) & m, (WB.z >> 4) & m, X1.x, X1.y);
+    imma_16832(d, WA.w & m, WB.w & m, (WA.w >> 4) & m, (WB.w >> 4) & m, X1.z, X1.w);
+    acc[0] = fmaf(fa, (float)d[0], acc[0]);
+    acc[1] = fmaf(fa, (float)d[1], acc[1]);
+    acc[2] = fmaf(fb, (float)d[2], acc[2]);
+    acc[3] = fmaf(fb, (float)d[3], acc[3]);
+}
+
+template <bool ZP>
 __global__ void __launch_bounds__(Shape<1>::threads, 1) gemv_w4a16_i8_kernel(const __grid_constant__ Params P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     using Sh = Shape<1>;
@@ -746,6 +860,7 @@ __global__ void __launch_bounds__(Shape<1>::threads, 1) gemv_w4a16_i8_kernel(con
         sm100::fence_barrier_init();
     }
     if (threadIdx.x < 64) S.ones[threadIdx.x] = 0x01010101u;
+    if (threadIdx.x < KC_W4A16_MAX_PROBLEMS) S.row_max[threadIdx.x] = 0u;
     __syncthreads();
 
     // prologue: scales and the first weight quads, before the wait on the
@@ -768,21 +883,30 @@ __global__ void __launch_bounds__(Shape<1>::threads, 1) gemv_w4a16_i8_kernel(con
     const uint32_t bar0 = sm100::smem_u32(&S.wfull[warp][0]);
     for (int s = 0; s < kRing; ++s)
         issue_quad(P, pf, ring0 + s * kQuad * kChunkBytes, bar0 + 8 * s, gw, leader);
+    // warm L2 with this CTA's share of the activations (128-byte lines L =
+    // blockIdx + gridDim * i over all problems) while the previous grid
+    // drains.  Only L2 is touched: the previous grid's writes land in L2, and
+    // the staging reads after the wait below see them.
+    {
+        int L = blockIdx.x + gridDim.x * threadIdx.x, pi = 0, base = 0;
+        while (pi < P.count && L >= base + (P.p[pi].K >> 6)) base += P.p[pi++].K >> 6;
+        if (pi < P.count)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(P.p[pi].x + (size_t)(L - base) * 64));
+    }
 
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    stage_i8(P, xs);
+    stage_i8<ZP>(P, S, xs);
     __syncthreads();
 
     // this lane's B column: planes for g < 3, the ones plane otherwise
     const uint32_t xs_u32 = sm100::smem_u32(xs);
     const uint32_t xlane = g < 3 ? xs_u32 + g * 64 + t * 16 : sm100::smem_u32(S.ones) + t * 16;
     const uint32_t xstep = g < 3 ? (uint32_t)kI8ChunkBytes : 0u;
-    // the record of chunk 0: this lane's two column seeds (columns 2t, 2t + 1;
-    // lanes t >= 2 hold columns no plane feeds) and the chunk factor f
+    // the seeds of chunk 0: this lane's two columns (2t, 2t + 1; lanes t >= 2
+    // hold columns no plane feeds)
     const uint32_t rec0 = xs_u32 + kI8RecOffset;
     const uint32_t seed_off = t == 0 ? 0u : 8u;
     const uint32_t ring_base = ring0 + g * 64 + 16 * t;
-    const uint32_t kMask = 0x0F0F0F0Fu;
     uint32_t it = 0, ti = 0;
     int pi = 0;
     for (int tile = first; tile < total; tile += stride, ++ti) {
@@ -796,7 +920,12 @@ __global__ void __launch_bounds__(Shape<1>::threads, 1) gemv_w4a16_i8_kernel(con
         const uint32_t sa_base = sm100::smem_u32(&S.scales[group][sb][g * G]);
         const uint32_t sb_base = sa_base + 16 * G;
         const uint32_t xp = xlane + xstep * (uint32_t)pr.sx_off;          // chunk 0 of this problem
-        const uint32_t recp = rec0 + (uint32_t)(kI8ChunkBytes * pr.sx_off);
+        const uint32_t recp = rec0 + (uint32_t)(kI8ChunkBytes * pr.sx_off) + seed_off;
+        // zero points of rows g and g + 8 (rows past N read the last row)
+        // (a problem without zero points in a launch that has some uses 8)
+        const bool has_z = ZP && pr.zeros != nullptr;
+        const uint8_t* za_row = has_z ? pr.zeros + (size_t)min(row0 + g, N - 1) * G : nullptr;
+        const uint8_t* zb_row = has_z ? pr.zeros + (size_t)min(row0 + g + 8, N - 1) * G : nullptr;
 
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         int c_begin, c_end;
@@ -806,32 +935,24 @@ __global__ void __launch_bounds__(Shape<1>::threads, 1) gemv_w4a16_i8_kernel(con
             const int nq = min(kQuad, c_end - q0);
             const uint32_t st = ring_base + s * (kQuad * kChunkBytes);
             sm100::mbar_wait(&S.wfull[warp][s], ph);
-#pragma unroll
-            for (int j = 0; j < kQuad; ++j) {
-                if (j < nq) {
-                    const uint32_t c = (uint32_t)(q0 + j);
-                    const uint32_t xa = xp + c * xstep;
-                    const uint4 X0 = lds128(xa), X1 = lds128(xa + 192);
-                    const uint32_t rec = recp + c * kI8ChunkBytes;
-                    const uint2 seed = lds64(rec + seed_off);
-                    const float f = __uint_as_float(lds32(rec + 16));
-                    const uint4 WA = lds128(st + j * kChunkBytes);
-                    const uint4 WB = lds128(st + j * kChunkBytes + 512);
-                    const int grp = (int)c >> gshift;
-                    const float fa = lds_half(sa_base + 2 * grp) * f;
-                    const float fb = lds_half(sb_base + 2 * grp) * f;
-                    int d[4] = {(int)seed.x, (int)seed.y, (int)seed.x, (int)seed.y};
-                    const uint32_t wa[4] = {WA.x, WA.y, WA.z, WA.w};
-                    const uint32_t wb[4] = {WB.x, WB.y, WB.z, WB.w};
-                    const uint32_t xb[8] = {X0.x, X0.y, X0.z, X0.w, X1.x, X1.y, X1.z, X1.w};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        imma_16832(d, wa[k] & kMask, wb[k] & kMask, (wa[k] >> 4) & kMask,
-                                   (wb[k] >> 4) & kMask, xb[2 * k], xb[2 * k + 1]);
-                    acc[0] = fmaf(fa, (float)d[0], acc[0]);
-                    acc[1] = fmaf(fa, (float)d[1], acc[1]);
-                    acc[2] = fmaf(fb, (float)d[2], acc[2]);
-                    acc[3] = fmaf(fb, (float)d[3], acc[3]);
+            const uint32_t c0 = (uint32_t)q0;
+            if (nq == kQuad) {   // a full stage: no per-chunk guard
+#pragma unroll 1
+                for (int j = 0; j < kQuad; ++j) {
+                    const uint32_t c = c0 + j, grp = c >> gshift;
+                    const int za = has_z ? (int)__ldg(za_row + grp) : 8;
+                    const int zb = has_z ? (int)__ldg(zb_row + grp) : 8;
+                    i8_chunk<ZP>(st + j * kChunkBytes, xp + c * xstep, recp + c * kI8ChunkBytes,
+                                 sa_base + 2 * grp, sb_base + 2 * grp, za, zb, acc);
+                }
+            } else {
+#pragma unroll 1
+                for (int j = 0; j < nq; ++j) {
+                    const uint32_t c = c0 + j, grp = c >> gshift;
+                    const int za = has_z ? (int)__ldg(za_row + grp) : 8;
+                    const int zb = has_z ? (int)__ldg(zb_row + grp) : 8;
+                    i8_chunk<ZP>(st + j * kChunkBytes, xp + c * xstep, recp + c * kI8ChunkBytes,
+                                 sa_base + 2 * grp, sb_base + 2 * grp, za, zb, acc);
                 }
             }
             __syncwarp();
@@ -880,7 +1001,7 @@ __global__ void __launch_bounds__(Shape<1>::threads, 1) gemv_w4a16_i8_kernel(con
                 float v = 0.f;
 #pragma unroll
                 for (int w = 0; w < kGroupWarps; ++w) v += S.red[group][slot][w][lane];
-                if (row0 + lane < N) pr.y[row0 + lane] = v;
+                if (row0 + lane < N) pr.y[row0 + lane] = v * S.row_f[pi];
             }
             __syncwarp();
             if (lane == 0) {
@@ -910,7 +1031,8 @@ __global__ void __launch_bounds__(256) gemv_w4a16_scalar(const __grid_constant__
         for (int c = lane; c < K; c += 32) {
             const uint8_t p = pr.packed[(size_t)r * (K / 2) + c / 2];
             const int u = (c & 1) ? (p >> 4) : (p & 15);
-            const float w = (float)(u - 8) * __half2float(pr.scales[(size_t)r * sc + c / P.gs]);
+            const int z = pr.zeros ? (int)(pr.zeros[(size_t)r * sc + c / P.gs] & 15) : 8;
+            const float w = (float)(u - z) * __half2float(pr.scales[(size_t)r * sc + c / P.gs]);
 #pragma unroll
             for (int m = 0; m < 16; ++m)
                 if (m < P.M) acc[m] = fmaf(w, __bfloat162float(pr.x[(size_t)m * K + c]), acc[m]);
@@ -954,9 +1076,10 @@ int launch_tc(const Params& P, size_t stage_bytes, cudaStream_t stream) {
 // Shared memory left for the staged activations and their chunk sums.
 constexpr size_t kSmemLimit = 227 * 1024;
 
+template <bool ZP>
 int launch_i8(const Params& P, size_t stage_bytes, cudaStream_t stream) {
     const size_t smem = fixed_smem_i8() + stage_bytes;
-    KC_CUDA_TRY(cudaFuncSetAttribute(gemv_w4a16_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    KC_CUDA_TRY(cudaFuncSetAttribute(gemv_w4a16_i8_kernel<ZP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem),
                 "gemv_w4a16_i8 shared-memory attribute");
     const int groups = (P.total_tiles + Shape<1>::groups - 1) / Shape<1>::groups;
@@ -970,13 +1093,14 @@ int launch_i8(const Params& P, size_t stage_bytes, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    KC_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_w4a16_i8_kernel, P), "gemv_w4a16_i8 launch");
+    KC_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_w4a16_i8_kernel<ZP>, P), "gemv_w4a16_i8 launch");
     return KC_OK;
 }
 
 int launch(Params& P, cudaStream_t stream) {
     if (P.total_tiles == 0) return KC_OK;
-    bool fast = true, single_group = true;
+    bool fast = true, single_group = true, any_zeros = false;
+    for (int i = 0; i < P.count; ++i) any_zeros = any_zeros || P.p[i].zeros != nullptr;
     for (int i = 0; i < P.count && fast; ++i) {
         const Prob& p = P.p[i];
         // TMA: 16-byte aligned base and row pitch; scale blocks: a tile's 16 rows
@@ -996,7 +1120,9 @@ int launch(Params& P, cudaStream_t stream) {
     P.gshift = gshift;
     P.magic = 0x43004300u;
     P.neg136 = 0xC308C308u;
-    if (!fast || gshift < 0) {
+    // zero points: the batch-1 integer path (below) takes them; the bf16
+    // paths do not, so other batch sizes run on the CUDA-core kernel
+    if (!fast || gshift < 0 || (any_zeros && P.M != 1)) {
         long rows = 0;
         for (int i = 0; i < P.count; ++i) rows += P.p[i].N;
         const long blocks = (rows + 7) / 8;
@@ -1024,9 +1150,19 @@ int launch(Params& P, cudaStream_t stream) {
         chunks += q.K / 128;
     }
     // batch 1: the integer tensor-core path when its staged byte planes fit
-    if (P.M == 1 && fixed_smem_i8() + (size_t)chunks * kI8ChunkBytes <= kSmemLimit) {
+    if (P.M == 1 && chunks <= kI8MaxChunks &&
+        fixed_smem_i8() + (size_t)chunks * kI8ChunkBytes <= kSmemLimit) {
         P.sx_chunks = (int)chunks;
-        return launch_i8(P, (size_t)chunks * kI8ChunkBytes, stream);
+        return any_zeros ? launch_i8<true>(P, (size_t)chunks * kI8ChunkBytes, stream)
+                         : launch_i8<false>(P, (size_t)chunks * kI8ChunkBytes, stream);
+    }
+    if (any_zeros) {   // batch 1 whose activations do not fit the staging: CUDA cores
+        long rows = 0;
+        for (int i = 0; i < P.count; ++i) rows += P.p[i].N;
+        const long blocks = (rows + 7) / 8;
+        const long cap = (long)kc::sm_count() * 8;
+        gemv_w4a16_scalar<<<(int)std::max(1L, std::min(blocks, cap)), 256, 0, stream>>>(P);
+        return kc::check_launch("gemv_w4a16_scalar");
     }
     const size_t fixed = NT == 1 ? fixed_smem<1>() : fixed_smem<2>();
     const size_t sx_bytes = (size_t)chunks * NT * 8 * 4;
@@ -1044,8 +1180,9 @@ KC_DEFINE_STATUS_READER(gemv)
 
 extern "C" {
 
-int kc_gemv_w4a16_grouped(const kc_w4a16_problem* problems, int count, int M, int gs,
-                          cudaStream_t stream) {
+namespace {
+int gemv_grouped(const kc_w4a16_problem* problems, const uint8_t* const* zeros, int count, int M,
+                 int gs, cudaStream_t stream) {
     KC_REQUIRE(problems != nullptr, KC_ERR_INVALID_ARG, "null problem list");
     KC_REQUIRE(count >= 1 && count <= KC_W4A16_MAX_PROBLEMS, KC_ERR_INVALID_ARG,
                "count=%d outside 1..%d", count, KC_W4A16_MAX_PROBLEMS);
@@ -1070,6 +1207,7 @@ int kc_gemv_w4a16_grouped(const kc_w4a16_problem* problems, int count, int M, in
                    "problem %d: bad shape N=%d K=%d for group_size=%d", order[i], q.N, q.K, gs);
         P.p[i].packed = q.packed;
         P.p[i].scales = reinterpret_cast<const __half*>(q.scales_f16);
+        P.p[i].zeros = zeros ? zeros[order[i]] : nullptr;
         P.p[i].x = reinterpret_cast<const __nv_bfloat16*>(q.x_bf16);
         P.p[i].y = q.y;
         P.p[i].N = q.N;
@@ -1081,11 +1219,31 @@ int kc_gemv_w4a16_grouped(const kc_w4a16_problem* problems, int count, int M, in
     P.total_tiles = (int)tiles;
     return launch(P, stream);
 }
+}  // namespace
+
+int kc_gemv_w4a16_grouped(const kc_w4a16_problem* problems, int count, int M, int gs,
+                          cudaStream_t stream) {
+    return gemv_grouped(problems, nullptr, count, M, gs, stream);
+}
+
+int kc_gemv_w4a16_grouped_zp(const kc_w4a16_problem* problems, const uint8_t* const* zeros,
+                             int count, int M, int gs, cudaStream_t stream) {
+    KC_REQUIRE(zeros != nullptr, KC_ERR_INVALID_ARG, "null zero-point list");
+    return gemv_grouped(problems, zeros, count, M, gs, stream);
+}
 
 int kc_gemv_w4a16(const uint8_t* packed, const uint16_t* scales_f16, const uint16_t* x_bf16,
                   float* y, int M, int N, int K, int gs, cudaStream_t stream) {
     kc_w4a16_problem p{packed, scales_f16, x_bf16, y, N, K};
-    return kc_gemv_w4a16_grouped(&p, 1, M, gs, stream);
+    return gemv_grouped(&p, nullptr, 1, M, gs, stream);
+}
+
+int kc_gemv_w4a16_zp(const uint8_t* packed, const uint16_t* scales_f16, const uint8_t* zeros,
+                     const uint16_t* x_bf16, float* y, int M, int N, int K, int gs,
+                     cudaStream_t stream) {
+    KC_REQUIRE(zeros != nullptr, KC_ERR_INVALID_ARG, "null zero points");
+    kc_w4a16_problem p{packed, scales_f16, x_bf16, y, N, K};
+    return gemv_grouped(&p, &zeros, 1, M, gs, stream);
 }
 
 }  // extern "C"

@@ -84,67 +84,93 @@ __global__ void dequant_int4_f32_vec(const uint8_t* __restrict__ packed,
     }
 }
 
-// fp32 GEMV over 16-byte chunks (32 weights of one group each), two rows
-// per warp so every x load serves both; a lane takes chunks lane, lane + 32,
-// ... in order and issues the packed loads of kU of them (both rows) before
-// it computes any, so a warp has 2 * kU * 512 bytes in flight instead of
-// 512.  Each row's accumulation order per lane is the one-row order, so the
-// result does not depend on the row pairing.
-__global__ void __launch_bounds__(256) gemv_int4_f32_vec(const uint8_t* __restrict__ packed,
-                                                         const float* __restrict__ scales,
-                                                         const uint8_t* __restrict__ zeros,
-                                                         const float* __restrict__ x,
-                                                         float* __restrict__ y, int rows, int cols,
-                                                         int gs) {
+// fp32 GEMV over 16-byte chunks (32 weights of one group each), one warp per
+// row: a lane takes chunks lane, lane + 32, ... and issues the loads of kU of
+// them before it computes any (kU * 16 bytes in flight per lane; a grid of
+// rows / 8 CTAs of eight warps fills every SM three or four times over).
+//
+// Dequantization without conversion instructions: a nibble u at bits 4e of a
+// word, for e <= 4, becomes the exact float 2^23 + 16^e * (u ^ 8) by one
+// LOP3 ((w & 0xF << 4e) ^ (0x4B000000 | 8 << 4e): the float's mantissa holds
+// the flipped nibble in place, its exponent is 2^23); subtracting the exact
+// constant 2^23 + (8 + z) * 16^e leaves (sx4(u) - z) * 16^e, the reference's
+// integer weight (quant_int4.cu:99-104) times 16^e, and one FMA accumulates it
+// against x in the accumulator of that power of 16.  Nibbles 5..7 come from
+// the word shifted right by 20 the same way.  Per chunk the five accumulators
+// combine as sum_e t_e * 16^-e (exact scalings) and the group scale
+// multiplies the result: the chunk's sum, then its scale, where the
+// reference scales every weight first -- fp32 GEMV parity is normwise.
+__device__ __forceinline__ float nib_f32(uint32_t w, int e) {  // 2^23 + 16^e * (u ^ 8)
+    return __uint_as_float((w & (0xFu << (4 * e))) ^ (0x4B000000u | (8u << (4 * e))));
+}
+
+__device__ __forceinline__ float chunk_dot(const uint4& v, const float4* xv, float z8) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float k[5], t[5];
+#pragma unroll
+    for (int e = 0; e < 5; ++e) {
+        k[e] = fmaf(z8, (float)(1 << (4 * e)), 8388608.f);
+        t[e] = 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float4 xa = __ldg(xv + 2 * q), xb = __ldg(xv + 2 * q + 1);
+        const float xe[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        const uint32_t h = w[q] >> 20;
+#pragma unroll
+        for (int e = 0; e < 5; ++e) t[e] = fmaf(nib_f32(w[q], e) - k[e], xe[e], t[e]);
+#pragma unroll
+        for (int e = 0; e < 3; ++e) t[e] = fmaf(nib_f32(h, e) - k[e], xe[5 + e], t[e]);
+    }
+    float c = t[4];
+#pragma unroll
+    for (int e = 3; e >= 0; --e) c = fmaf(c, 0.0625f, t[e]);
+    return c;
+}
+
+__global__ void __launch_bounds__(256, 4) gemv_int4_f32_vec(const uint8_t* __restrict__ packed,
+                                                            const float* __restrict__ scales,
+                                                            const uint8_t* __restrict__ zeros,
+                                                            const float* __restrict__ x,
+                                                            float* __restrict__ y, int rows, int cols,
+                                                            int gs, int gs_shift) {
     constexpr int kU = 4;
     const int lane = threadIdx.x & 31;
-    const int warps = (gridDim.x * blockDim.x) >> 5;
-    const int sc = cols / gs, cpr = cols / 32;
-    for (int r0 = 2 * ((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r0 < rows; r0 += 2 * warps) {
-        const bool two = r0 + 1 < rows;
-        const int r1 = two ? r0 + 1 : r0;     // a lone last row computes itself twice
-        const uint8_t* p0 = packed + (long)r0 * (cols / 2);
-        const uint8_t* p1 = packed + (long)r1 * (cols / 2);
-        float acc0 = 0.f, acc1 = 0.f;
-        for (int jb = lane; jb < cpr; jb += 32 * kU) {
-            uint4 v0[kU], v1[kU];
+    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (r >= rows) return;
+    const int sc = cols / gs, cpr = cols / 32, zc = sc / 2;  // the reference's floor zero stride
+    const uint8_t* p = packed + (long)r * (cols / 2);
+    const float* srow = scales + (long)r * sc;
+    const uint8_t* zrow = zeros + (long)r * zc;
+    float acc = 0.f;
+    for (int jb = lane; jb < cpr; jb += 32 * kU) {
+        // every global load of the kU chunks (weights, scales, zero points)
+        // is in flight before the first chunk is computed
+        uint4 v[kU];
+        float s[kU];
+        uint32_t zb[kU];
+        int g[kU];
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int j = jb + 32 * u;
-                if (j < cpr) {
-                    v0[u] = kc_ldg_stream(p0 + 16 * j);
-                    v1[u] = kc_ldg_stream(p1 + 16 * j);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int j = jb + 32 * u;
-                if (j >= cpr) break;
-                const int g = (32 * j) / gs;
-                const float s0 = scales[(long)r0 * sc + g], s1 = scales[(long)r1 * sc + g];
-                const int z0 = ref_zp(zeros, r0, cols, gs, g), z1 = ref_zp(zeros, r1, cols, gs, g);
-                const uint32_t w0[4] = {v0[u].x, v0[u].y, v0[u].z, v0[u].w};
-                const uint32_t w1[4] = {v1[u].x, v1[u].y, v1[u].z, v1[u].w};
-                const float4* xv = reinterpret_cast<const float4*>(x + 32 * j);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 xa = __ldg(xv + 2 * q), xb = __ldg(xv + 2 * q + 1);
-                    const float xe[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        acc0 = fmaf((float)(sx4((w0[q] >> (4 * e)) & 15u) - z0) * s0, xe[e], acc0);
-                        acc1 = fmaf((float)(sx4((w1[q] >> (4 * e)) & 15u) - z1) * s1, xe[e], acc1);
-                    }
-                }
+        for (int u = 0; u < kU; ++u) {
+            const int j = jb + 32 * u;
+            if (j < cpr) {
+                g[u] = gs_shift >= 0 ? (32 * j) >> gs_shift : (32 * j) / gs;
+                v[u] = kc_ldg_stream(p + 16 * j);
+                s[u] = __ldg(srow + g[u]);
+                zb[u] = __ldg(zrow + (g[u] >> 1));
             }
         }
-        acc0 = kc_warp_sum(acc0);
-        acc1 = kc_warp_sum(acc1);
-        if (lane == 0) {
-            y[r0] = acc0;
-            if (two) y[r1] = acc1;
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int j = jb + 32 * u;
+            if (j >= cpr) break;
+            const uint32_t z = (g[u] & 1) ? (zb[u] >> 4) : (zb[u] & 15u);
+            acc = fmaf(s[u], chunk_dot(v[u], reinterpret_cast<const float4*>(x + 32 * j), (float)(8 + z)),
+                       acc);
         }
     }
+    acc = kc_warp_sum(acc);
+    if (lane == 0) y[r] = acc;
 }
 
 // fp32 GEMV, one warp per row, one packed byte per lane and step: any shape
@@ -183,8 +209,10 @@ __global__ void __launch_bounds__(256) gemv_int4_f32_bytes(const uint8_t* __rest
 // ---------------------------------------------------------------------------
 
 // bf16 dequant, one thread per 16-byte chunk (32 weights of one group).
+// zeros: per-group zero points u8[N, K/gs] (null: 8)
 __global__ void dequant_w4_bf16_vec(const uint8_t* __restrict__ packed,
                                     const __half* __restrict__ scales,
+                                    const uint8_t* __restrict__ zeros,
                                     __nv_bfloat16* __restrict__ out, int N, int K, int gs) {
     const int cpr = K / 32;
     const long nchunks = (long)N * cpr;
@@ -194,6 +222,7 @@ __global__ void dequant_w4_bf16_vec(const uint8_t* __restrict__ packed,
         const int r = (int)(i / cpr);
         const int j = (int)(i - (long)r * cpr);
         const float s = __half2float(scales[(long)r * sc + (32 * j) / gs]);
+        const int z = zeros ? (int)(zeros[(long)r * sc + (32 * j) / gs] & 15) : 8;
         const uint4 v = kc_ldg_stream(packed + i * 16);
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint4* dst = reinterpret_cast<uint4*>(out + (long)r * K + 32 * j);
@@ -202,8 +231,8 @@ __global__ void dequant_w4_bf16_vec(const uint8_t* __restrict__ packed,
             uint32_t o[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float lo = (float)((int)((w[q] >> (8 * e)) & 15u) - 8) * s;
-                const float hi = (float)((int)((w[q] >> (8 * e + 4)) & 15u) - 8) * s;
+                const float lo = (float)((int)((w[q] >> (8 * e)) & 15u) - z) * s;
+                const float hi = (float)((int)((w[q] >> (8 * e + 4)) & 15u) - z) * s;
                 __nv_bfloat162 h2 = __floats2bfloat162_rn(lo, hi);
                 o[e] = *reinterpret_cast<uint32_t*>(&h2);
             }
@@ -214,6 +243,7 @@ __global__ void dequant_w4_bf16_vec(const uint8_t* __restrict__ packed,
 
 __global__ void dequant_w4_bf16_scalar(const uint8_t* __restrict__ packed,
                                        const __half* __restrict__ scales,
+                                       const uint8_t* __restrict__ zeros,
                                        __nv_bfloat16* __restrict__ out, int N, int K, int gs) {
     const long n = (long)N * K;
     const int sc = K / gs;
@@ -223,7 +253,8 @@ __global__ void dequant_w4_bf16_scalar(const uint8_t* __restrict__ packed,
         const int c = (int)(i - (long)r * K);
         const uint8_t p = packed[(long)r * (K / 2) + c / 2];
         const int u = (c & 1) ? (p >> 4) : (p & 15);
-        const float w = (float)(u - 8) * __half2float(scales[(long)r * sc + c / gs]);
+        const int z = zeros ? (int)(zeros[(long)r * sc + c / gs] & 15) : 8;
+        const float w = (float)(u - z) * __half2float(scales[(long)r * sc + c / gs]);
         out[i] = __float2bfloat16_rn(w);
     }
 }
@@ -279,8 +310,14 @@ int kc_gemv_int4_f32(const uint8_t* packed, const float* scales, const uint8_t* 
     const bool vec = (cols % 32 == 0) && (gs % 32 == 0) && kc::aligned(packed, 16) &&
                      kc::aligned(x, 16);
     if (vec) {
-        const int grid2 = grid_for(((long)rows + 15) / 16, 256);   // 8 warps x 2 rows per CTA
-        gemv_int4_f32_vec<<<grid2, 256, 0, stream>>>(packed, scales, zeros, x, y, rows, cols, gs);
+        // 8 rows per CTA, one CTA per 8 rows (no grid-stride loop)
+        const long ctas = ((long)rows + 7) / 8;
+        KC_REQUIRE(ctas < (1L << 31), KC_ERR_INVALID_ARG, "too many rows");
+        int gs_shift = -1;
+        for (int b = 0; b < 31; ++b)
+            if (gs == (1 << b)) gs_shift = b;
+        gemv_int4_f32_vec<<<(unsigned)ctas, 256, 0, stream>>>(packed, scales, zeros, x, y, rows, cols, gs,
+                                                             gs_shift);
         return kc::check_launch("gemv_int4_f32");
     }
     const int grid = grid_for(((long)rows + 7) / 8, 256);
@@ -304,8 +341,9 @@ void launch_gemv_int4(const uint8_t* d_packed, const float* d_scales, const uint
         kc::check_cuda(cudaStreamSynchronize(stream), "launch_gemv_int4 sync");
 }
 
-int kc_dequantize_w4_bf16(const uint8_t* packed, const uint16_t* scales_f16, uint16_t* out_bf16,
-                          int N, int K, int gs, cudaStream_t stream) {
+namespace {
+int dequantize_w4_bf16(const uint8_t* packed, const uint16_t* scales_f16, const uint8_t* zeros,
+                       uint16_t* out_bf16, int N, int K, int gs, cudaStream_t stream) {
     KC_REQUIRE(packed && scales_f16 && out_bf16, KC_ERR_INVALID_ARG, "null pointer argument");
     KC_REQUIRE(N >= 0 && K >= 0 && K % 2 == 0, KC_ERR_INVALID_ARG, "bad shape N=%d K=%d", N, K);
     KC_REQUIRE(gs > 0 && K % gs == 0, KC_ERR_INVALID_ARG, "group_size=%d must divide K=%d", gs, K);
@@ -314,12 +352,26 @@ int kc_dequantize_w4_bf16(const uint8_t* packed, const uint16_t* scales_f16, uin
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out_bf16);
     if (K % 32 == 0 && gs % 32 == 0 && kc::aligned(packed, 16) && kc::aligned(out_bf16, 16)) {
         const long n = (long)N * (K / 32);
-        dequant_w4_bf16_vec<<<grid_for((n + 255) / 256, 256), 256, 0, stream>>>(packed, s, o, N, K, gs);
+        dequant_w4_bf16_vec<<<grid_for((n + 255) / 256, 256), 256, 0, stream>>>(packed, s, zeros, o, N,
+                                                                                 K, gs);
     } else {
         const long n = (long)N * K;
-        dequant_w4_bf16_scalar<<<grid_for((n + 255) / 256, 256), 256, 0, stream>>>(packed, s, o, N, K, gs);
+        dequant_w4_bf16_scalar<<<grid_for((n + 255) / 256, 256), 256, 0, stream>>>(packed, s, zeros, o,
+                                                                                    N, K, gs);
     }
     return kc::check_launch("dequantize_w4_bf16");
+}
+}  // namespace
+
+int kc_dequantize_w4_bf16(const uint8_t* packed, const uint16_t* scales_f16, uint16_t* out_bf16,
+                          int N, int K, int gs, cudaStream_t stream) {
+    return dequantize_w4_bf16(packed, scales_f16, nullptr, out_bf16, N, K, gs, stream);
+}
+
+int kc_dequantize_w4_bf16_zp(const uint8_t* packed, const uint16_t* scales_f16, const uint8_t* zeros,
+                             uint16_t* out_bf16, int N, int K, int gs, cudaStream_t stream) {
+    KC_REQUIRE(zeros != nullptr, KC_ERR_INVALID_ARG, "null zero points");
+    return dequantize_w4_bf16(packed, scales_f16, zeros, out_bf16, N, K, gs, stream);
 }
 
 }  // extern "C"

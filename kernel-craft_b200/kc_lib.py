@@ -83,8 +83,11 @@ _PROTOS = [
     ("kc_dequantize_int4_f32", ci, [vp, vp, vp, vp, ci, ci, ci, vp]),
     ("kc_gemv_int4_f32", ci, [vp, vp, vp, vp, vp, ci, ci, ci, vp]),
     ("kc_dequantize_w4_bf16", ci, [vp, vp, vp, ci, ci, ci, vp]),
+    ("kc_dequantize_w4_bf16_zp", ci, [vp, vp, vp, vp, ci, ci, ci, vp]),
     ("kc_gemv_w4a16", ci, [vp, vp, vp, vp, ci, ci, ci, ci, vp]),
     ("kc_gemv_w4a16_grouped", ci, [ctypes.POINTER(W4A16Problem), ci, ci, ci, vp]),
+    ("kc_gemv_w4a16_zp", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, vp]),
+    ("kc_gemv_w4a16_grouped_zp", ci, [ctypes.POINTER(W4A16Problem), ctypes.POINTER(vp), ci, ci, ci, vp]),
     ("kc_quantize_fp8_per_token", ci, [vp, vp, vp, ci, ci, vp]),
     ("kc_quantize_fp8_per_channel", ci, [vp, vp, vp, ci, ci, vp]),
     ("kc_quantize_fp8_per_tensor", ci, [vp, vp, vp, cl, vp]),
@@ -97,6 +100,7 @@ _PROTOS = [
     ("kc_gemm_fp8", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16_act", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, vp]),
+    ("kc_gemm_w4a16_zp", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16_allgather", ci, [vp, vp, vp, ctypes.POINTER(vp), ci, ci, ci, ci, ci, ci, vp]),
     ("kc_allreduce_bf16_peer", ci, [ctypes.POINTER(vp), ctypes.POINTER(vp), ci, ci, cl, vp]),
     ("kc_peer_barrier", ci, [ctypes.POINTER(vp), ci, ci, ci, ctypes.c_uint64, vp, vp]),

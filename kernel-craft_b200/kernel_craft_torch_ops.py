@@ -206,30 +206,51 @@ def fp8_quantize_per_channel(w) -> Tuple[torch.Tensor, torch.Tensor]:
     return q, scales
 
 
-def w4a16_dequantize(packed, scales_f16, group_size: int = 128):
-    """GPTQ W4 (implicit zero-point 8, fp16 scales) -> bf16 [N, K]."""
+def _check_zeros(zeros, n, k, group_size, name=""):
+    """Per-group zero points: u8 [N, K/gs] (one 0..15 value per byte), or None."""
+    if zeros is None:
+        return None
+    zeros = zeros.contiguous()
+    _expect(zeros, f"{name}zeros", shape=(n, k // group_size), dtypes=(torch.uint8,))
+    return zeros
+
+
+def w4a16_dequantize(packed, scales_f16, group_size: int = 128, zeros=None):
+    """W4 -> bf16 [N, K]: bf16((u - z) * s), z = 8 (GPTQ symmetric) unless
+    per-group zero points zeros u8 [N, K/gs] are given (AWQ, asymmetric GPTQ)."""
     packed, scales_f16 = packed.contiguous(), scales_f16.contiguous()
     n, k = _check_w4(packed, scales_f16, group_size)
-    _require_cuda(packed, scales_f16)
+    zeros = _check_zeros(zeros, n, k, group_size)
+    _require_cuda(packed, scales_f16, *([zeros] if zeros is not None else []))
     out = torch.empty(n, k, dtype=torch.bfloat16, device=packed.device)
-    check(lib().kc_dequantize_w4_bf16(_ptr(packed), _ptr(scales_f16), _ptr(out), n, k,
-                                      group_size, _stream()))
+    if zeros is None:
+        check(lib().kc_dequantize_w4_bf16(_ptr(packed), _ptr(scales_f16), _ptr(out), n, k,
+                                          group_size, _stream()))
+    else:
+        check(lib().kc_dequantize_w4_bf16_zp(_ptr(packed), _ptr(scales_f16), _ptr(zeros), _ptr(out),
+                                             n, k, group_size, _stream()))
     return out
 
 
-def w4a16_gemv(packed, scales_f16, x, group_size: int = 128):
-    """y[M, N] (fp32) = x[M, K] (bf16, M <= 16) . W^T with W the GPTQ W4 [N, K]."""
+def w4a16_gemv(packed, scales_f16, x, group_size: int = 128, zeros=None):
+    """y[M, N] (fp32) = x[M, K] (bf16, M <= 16) . W^T with W the W4 [N, K]
+    (zero point 8, or per-group zero points zeros u8 [N, K/gs])."""
     packed, scales_f16, x = packed.contiguous(), scales_f16.contiguous(), x.contiguous()
     if x.dim() == 1:
         x = x.unsqueeze(0)
     n, k = _check_w4(packed, scales_f16, group_size)
+    zeros = _check_zeros(zeros, n, k, group_size)
     _expect(x, "x", shape=(x.shape[0], k), dtypes=_BF16)
-    _require_cuda(packed, scales_f16, x)
+    _require_cuda(packed, scales_f16, x, *([zeros] if zeros is not None else []))
     m = x.shape[0]
     y = torch.empty(m, n, dtype=torch.float32, device=packed.device)
     with kernel_span("w4a16_gemv", rows=n, cols=k, batch=m, group_size=group_size):
-        check(lib().kc_gemv_w4a16(_ptr(packed), _ptr(scales_f16), _ptr(x), _ptr(y), m, n, k,
-                                  group_size, _stream()))
+        if zeros is None:
+            check(lib().kc_gemv_w4a16(_ptr(packed), _ptr(scales_f16), _ptr(x), _ptr(y), m, n, k,
+                                      group_size, _stream()))
+        else:
+            check(lib().kc_gemv_w4a16_zp(_ptr(packed), _ptr(scales_f16), _ptr(zeros), _ptr(x),
+                                         _ptr(y), m, n, k, group_size, _stream()))
     return y
 
 
@@ -267,16 +288,18 @@ _ACTIVATIONS = {"none": kc_lib.KC_ACT_NONE, "gelu_quick": kc_lib.KC_ACT_GELU_QUI
 
 
 def w4a16_gemm(x, packed, scales_f16, group_size: int = 128, out_dtype=torch.bfloat16,
-               activation: str = "none"):
+               activation: str = "none", zeros=None):
     """C[M, N] = act(x[M, K] (bf16) . W^T) on the tcgen05 tensor cores, W the
     GPTQ W4 [N, K] (packed u8 [N, K/2], fp16 scales [N, K/gs]); fp32
     accumulation, bf16 (default) or fp32 output.  activation "gelu_quick"
     applies x * sigmoid(1.702 x), the reference MLP block's GELU
-    (examples/python/transformer/tensor_parallel.py:162), in the epilogue."""
+    (examples/python/transformer/tensor_parallel.py:162), in the epilogue.
+    zeros: per-group zero points u8 [N, K/gs] (AWQ, asymmetric GPTQ)."""
     if activation not in _ACTIVATIONS:
         raise ValueError(f"activation must be one of {sorted(_ACTIVATIONS)}")
     x, packed, scales_f16 = x.contiguous(), packed.contiguous(), scales_f16.contiguous()
     n, k = _check_w4(packed, scales_f16, group_size)
+    zeros = _check_zeros(zeros, n, k, group_size)
     if x.dim() != 2 or x.shape[1] != k:
         raise ValueError(f"x must be [M, {k}] (the packed weights' K), got {tuple(x.shape)}")
     _expect(x, "x", dtypes=_BF16)
@@ -286,9 +309,15 @@ def w4a16_gemm(x, packed, scales_f16, group_size: int = 128, out_dtype=torch.bfl
     m = x.shape[0]
     out = torch.empty(m, n, dtype=out_dtype, device=x.device)
     with kernel_span("w4a16_gemm", rows=n, cols=k, batch=m, group_size=group_size):
-        check(lib().kc_gemm_w4a16_act(_ptr(x), _ptr(packed), _ptr(scales_f16), _ptr(out),
-                                      1 if out_dtype == torch.float32 else 0, m, n, k, group_size,
-                                      n, _ACTIVATIONS[activation], _stream()))
+        if zeros is None:
+            check(lib().kc_gemm_w4a16_act(_ptr(x), _ptr(packed), _ptr(scales_f16), _ptr(out),
+                                          1 if out_dtype == torch.float32 else 0, m, n, k,
+                                          group_size, n, _ACTIVATIONS[activation], _stream()))
+        else:
+            _require_cuda(zeros)
+            check(lib().kc_gemm_w4a16_zp(_ptr(x), _ptr(packed), _ptr(scales_f16), _ptr(zeros),
+                                         _ptr(out), 1 if out_dtype == torch.float32 else 0, m, n,
+                                         k, group_size, n, _ACTIVATIONS[activation], _stream()))
     return out
 
 

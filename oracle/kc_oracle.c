@@ -155,24 +155,40 @@ ORA_EXPORT float ora_gptq_weight(uint8_t p, int high, uint16_t scale_f16) {
     return (float)(u - 8) * ora_half_to_float(scale_f16);
 }
 
-/* bf16 dequant of GPTQ weights: out[r,c] = bf16_rne((u-8) * float(s_f16)). */
-ORA_EXPORT void ora_dequantize_w4_bf16(const uint8_t* packed, const uint16_t* scales_f16,
-                                       uint16_t* out, int rows, int cols, int gs) {
+/* bf16 dequant of W4 weights with per-group zero points (AWQ, asymmetric
+ * GPTQ): out[r,c] = bf16_rne((u - z) * float(s_f16)), z = zeros[r, c/gs]
+ * (one byte per group, 0..15); zeros == NULL is the symmetric GPTQ case z = 8,
+ * the reference's dequantize_int4 of packed ^ 0x88 with zero points 0
+ * (quant_int4.cu:99-104). */
+static int ora_w4_zp(const uint8_t* zeros, long row, int sc, int g) {
+    return zeros ? (int)(zeros[row * sc + g] & 0xF) : 8;
+}
+
+ORA_EXPORT void ora_dequantize_w4_bf16_zp(const uint8_t* packed, const uint16_t* scales_f16,
+                                          const uint8_t* zeros, uint16_t* out, int rows, int cols,
+                                          int gs) {
     int sc = cols / gs;
     #pragma omp parallel for schedule(static)
     for (int r = 0; r < rows; ++r)
         for (int c = 0; c < cols; ++c) {
             uint8_t p = packed[(long)r * (cols / 2) + c / 2];
-            float w = ora_gptq_weight(p, c & 1, scales_f16[(long)r * sc + c / gs]);
+            int u = (c & 1) ? ((p >> 4) & 0xF) : (p & 0xF);
+            float w = (float)(u - ora_w4_zp(zeros, r, sc, c / gs)) *
+                      ora_half_to_float(scales_f16[(long)r * sc + c / gs]);
             out[(long)r * cols + c] = ora_float_to_bf16(w);
         }
 }
 
-/* W4A16 GEMV: y[m, r] = sum_c w(r,c) * float(x_bf16[m, c]), double accumulate.
- * M activation rows, N = rows of W, K = cols. */
-ORA_EXPORT void ora_gemv_w4a16(const uint8_t* packed, const uint16_t* scales_f16,
-                               const uint16_t* x_bf16, float* y,
-                               int M, int N, int K, int gs) {
+ORA_EXPORT void ora_dequantize_w4_bf16(const uint8_t* packed, const uint16_t* scales_f16,
+                                       uint16_t* out, int rows, int cols, int gs) {
+    ora_dequantize_w4_bf16_zp(packed, scales_f16, NULL, out, rows, cols, gs);
+}
+
+/* W4A16 GEMV, y[m,n] = sum_k w[n,k] x[m,k] with w = (u - z) * s as above,
+ * accumulated in double (the truth the kernels are checked against). */
+ORA_EXPORT void ora_gemv_w4a16_zp(const uint8_t* packed, const uint16_t* scales_f16,
+                                  const uint8_t* zeros, const uint16_t* x_bf16, float* y,
+                                  int M, int N, int K, int gs) {
     int sc = K / gs;
     #pragma omp parallel for schedule(static)
     for (int r = 0; r < N; ++r) {
@@ -180,10 +196,11 @@ ORA_EXPORT void ora_gemv_w4a16(const uint8_t* packed, const uint16_t* scales_f16
         int mm = M;
         for (int g = 0; g < sc; ++g) {
             float s = ora_half_to_float(scales_f16[(long)r * sc + g]);
+            int z = ora_w4_zp(zeros, r, sc, g);
             for (int c = g * gs; c < (g + 1) * gs; ++c) {
                 uint8_t p = packed[(long)r * (K / 2) + c / 2];
                 int u = (c & 1) ? (p >> 4) : (p & 0xF);
-                double w = (double)((float)(u - 8) * s);
+                double w = (double)((float)(u - z) * s);
                 for (int m = 0; m < mm; ++m)
                     acc[m] += w * (double)ora_bf16_to_float(x_bf16[(long)m * K + c]);
             }
@@ -191,6 +208,12 @@ ORA_EXPORT void ora_gemv_w4a16(const uint8_t* packed, const uint16_t* scales_f16
         for (int m = 0; m < mm; ++m) y[(long)m * N + r] = (float)acc[m];
         free(acc);
     }
+}
+
+ORA_EXPORT void ora_gemv_w4a16(const uint8_t* packed, const uint16_t* scales_f16,
+                               const uint16_t* x_bf16, float* y,
+                               int M, int N, int K, int gs) {
+    ora_gemv_w4a16_zp(packed, scales_f16, NULL, x_bf16, y, M, N, K, gs);
 }
 
 /* ------------------------------------------------------------------------- */
@@ -324,9 +347,9 @@ ORA_EXPORT void ora_gemm_fp8_rowcol(const uint8_t* a_codes, const float* sa,
 
 /* W4A16 GEMM reference: C[m, n] = sum_k float(A_bf16[m,k]) * w(n,k),
  * w the GPTQ weight above; double accumulate. */
-ORA_EXPORT void ora_gemm_w4a16(const uint16_t* A_bf16, const uint8_t* packed,
-                               const uint16_t* scales_f16, float* C,
-                               int M, int N, int K, int gs) {
+ORA_EXPORT void ora_gemm_w4a16_zp(const uint16_t* A_bf16, const uint8_t* packed,
+                                  const uint16_t* scales_f16, const uint8_t* zeros, float* C,
+                                  int M, int N, int K, int gs) {
     int sc = K / gs;
     #pragma omp parallel for schedule(static)
     for (int n = 0; n < N; ++n) {
@@ -336,7 +359,8 @@ ORA_EXPORT void ora_gemm_w4a16(const uint16_t* A_bf16, const uint8_t* packed,
         for (int k = 0; k < kk; ++k) {
             uint8_t p = packed[(long)n * (K / 2) + k / 2];
             int u = (k & 1) ? (p >> 4) : (p & 0xF);
-            wrow[k] = (float)(u - 8) * ora_half_to_float(scales_f16[(long)n * sc + k / gs]);
+            wrow[k] = (float)(u - ora_w4_zp(zeros, n, sc, k / gs)) *
+                      ora_half_to_float(scales_f16[(long)n * sc + k / gs]);
         }
         for (int m = 0; m < M; ++m) {
             double acc = 0.0;
@@ -346,6 +370,12 @@ ORA_EXPORT void ora_gemm_w4a16(const uint16_t* A_bf16, const uint8_t* packed,
         }
         free(wrow);
     }
+}
+
+ORA_EXPORT void ora_gemm_w4a16(const uint16_t* A_bf16, const uint8_t* packed,
+                               const uint16_t* scales_f16, float* C,
+                               int M, int N, int K, int gs) {
+    ora_gemm_w4a16_zp(A_bf16, packed, scales_f16, NULL, C, M, N, K, gs);
 }
 
 /* launch_ring_allreduce: tensor_parallel.cu:93-142.  Chunk c (size

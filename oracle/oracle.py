@@ -42,7 +42,9 @@ def lib() -> ctypes.CDLL:
             "ora_gemv_int4": (None, [_vp] * 5 + [_ci] * 3),
             "ora_float_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),
             "ora_dequantize_w4_bf16": (None, [_vp] * 3 + [_ci] * 3),
+            "ora_dequantize_w4_bf16_zp": (None, [_vp] * 4 + [_ci] * 3),
             "ora_gemv_w4a16": (None, [_vp] * 4 + [_ci] * 4),
+            "ora_gemv_w4a16_zp": (None, [_vp] * 5 + [_ci] * 4),
             "ora_e4m3_encode": (ctypes.c_uint8, [ctypes.c_float]),
             "ora_e4m3_decode": (ctypes.c_float, [ctypes.c_uint8]),
             "ora_e4m3_encode_array": (None, [_vp, _vp, _cl, _ci]),
@@ -53,6 +55,7 @@ def lib() -> ctypes.CDLL:
             "ora_gemm_nt_f32": (None, [_vp] * 3 + [_ci] * 3),
             "ora_gemm_fp8_rowcol": (None, [_vp] * 5 + [_ci] * 3),
             "ora_gemm_w4a16": (None, [_vp] * 4 + [_ci] * 4),
+            "ora_gemm_w4a16_zp": (None, [_vp] * 5 + [_ci] * 4),
             "ora_ring_allreduce": (None, [_vp, _ci, _ci]),
             "ora_allgather": (None, [_vp, _vp, _ci, _ci]),
             "ora_num_threads": (_ci, []),
@@ -92,30 +95,46 @@ def gemv_int4(packed, scales, zeros, x, rows, cols, gs) -> np.ndarray:
 # GPTQ W4A16 (implicit zero-point 8, fp16 scales, bf16 activations)
 # --------------------------------------------------------------------------
 
-def dequantize_w4_bf16(packed, scales_f16, N, K, gs) -> np.ndarray:
-    """Returns the bf16 bit patterns (uint16) of the dequantized weights."""
+def _zeros(zeros, N, K, gs):
+    """Per-group zero points as a contiguous u8 [N, K/gs] array, or None (symmetric, 8)."""
+    if zeros is None:
+        return None
+    z = _c(zeros, np.uint8)
+    assert z.shape == (N, K // gs), z.shape
+    return z
+
+
+def dequantize_w4_bf16(packed, scales_f16, N, K, gs, zeros=None) -> np.ndarray:
+    """Returns the bf16 bit patterns (uint16) of the dequantized weights
+    bf16((u - z) * s); zeros None means z = 8 (symmetric GPTQ)."""
     packed = _c(packed, np.uint8)
     s = _c(np.asarray(scales_f16).view(np.uint16), np.uint16)
+    z = _zeros(zeros, N, K, gs)
     out = np.empty((N, K), np.uint16)
-    lib().ora_dequantize_w4_bf16(_p(packed), _p(s), _p(out), N, K, gs)
+    lib().ora_dequantize_w4_bf16_zp(_p(packed), _p(s), _p(z) if z is not None else None, _p(out),
+                                    N, K, gs)
     return out
 
 
-def gemv_w4a16(packed, scales_f16, x_bf16_bits, M, N, K, gs) -> np.ndarray:
+def gemv_w4a16(packed, scales_f16, x_bf16_bits, M, N, K, gs, zeros=None) -> np.ndarray:
     packed = _c(packed, np.uint8)
     s = _c(np.asarray(scales_f16).view(np.uint16), np.uint16)
     x = _c(x_bf16_bits, np.uint16)
+    z = _zeros(zeros, N, K, gs)
     y = np.empty((M, N), np.float32)
-    lib().ora_gemv_w4a16(_p(packed), _p(s), _p(x), _p(y), M, N, K, gs)
+    lib().ora_gemv_w4a16_zp(_p(packed), _p(s), _p(z) if z is not None else None, _p(x), _p(y),
+                            M, N, K, gs)
     return y
 
 
-def gemm_w4a16(a_bf16_bits, packed, scales_f16, M, N, K, gs) -> np.ndarray:
+def gemm_w4a16(a_bf16_bits, packed, scales_f16, M, N, K, gs, zeros=None) -> np.ndarray:
     a = _c(a_bf16_bits, np.uint16)
     packed = _c(packed, np.uint8)
     s = _c(np.asarray(scales_f16).view(np.uint16), np.uint16)
+    z = _zeros(zeros, N, K, gs)
     c = np.empty((M, N), np.float32)
-    lib().ora_gemm_w4a16(_p(a), _p(packed), _p(s), _p(c), M, N, K, gs)
+    lib().ora_gemm_w4a16_zp(_p(a), _p(packed), _p(s), _p(z) if z is not None else None, _p(c),
+                            M, N, K, gs)
     return c
 
 

@@ -33,11 +33,18 @@ def _dequant_checkpoint(u, s, z, g_of_k):
 
 
 def _dequant_w4a16(w: C.W4A16Weights, gs):
+    """The converted weights as the library's kernels read them: (u - z) * s,
+    z = 8 when the conversion found no zero points (checked against the
+    oracle's dequantization of the same layout)."""
     N, half = w.packed.shape
     u = np.empty((N, 2 * half), np.float32)
     u[:, 0::2] = w.packed & 15
     u[:, 1::2] = w.packed >> 4
-    return (u - 8.0) * np.repeat(w.scales.astype(np.float32), gs, axis=1)
+    z = 8.0 if w.zeros is None else np.repeat(w.zeros.astype(np.float32), gs, axis=1)
+    out = (u - z) * np.repeat(w.scales.astype(np.float32), gs, axis=1)
+    bf = O.bf16_bits_to_f32(O.dequantize_w4_bf16(w.packed, w.scales, N, 2 * half, gs, zeros=w.zeros))
+    np.testing.assert_array_equal(bf, O.bf16_bits_to_f32(O.f32_to_bf16_bits(out)))
+    return out
 
 
 def _pack_rows(q):            # restated pack_rows: k = 8i + j in bits 4j of word [i, n]
@@ -127,13 +134,46 @@ def test_awq(packers, K, N, gs):
     np.testing.assert_array_equal(_dequant_w4a16(w, gs), _dequant_checkpoint(u, s, z, np.arange(K) // gs))
 
 
-def test_asymmetric_zero_points_rejected(packers):
-    K, N, gs = 256, 32, 128
-    u, s, z = _inputs(K, N, gs, seed=7, zero=None)
-    with pytest.raises(ValueError, match="zero points"):
-        C.from_gptq(packers[0](u), packers[1](z), s, group_size=gs, checkpoint_format="gptq_v2")
-    with pytest.raises(ValueError, match="zero points"):
-        C.from_awq(packers[2](u), packers[2](z), s, group_size=gs)
+@pytest.mark.parametrize("K,N,gs", [(256, 32, 128), (384, 24, 128), (512, 16, 64)])
+def test_asymmetric_zero_points_convert(packers, K, N, gs):
+    """AWQ and asymmetric GPTQ: the zero points come along, u8 [N, K/gs], and
+    the converted weights dequantize to exactly (q - z) * s."""
+    u, s, z = _inputs(K, N, gs, seed=7 + K, zero=None)
+    g = np.arange(K) // gs
+    w = C.from_gptq(packers[0](u), packers[1](z), s, group_size=gs, checkpoint_format="gptq_v2")
+    assert w.zeros is not None and w.zeros.shape == (N, K // gs) and w.zeros.dtype == np.uint8
+    np.testing.assert_array_equal(_dequant_w4a16(w, gs), _dequant_checkpoint(u, s, z, g))
+    w1 = C.from_gptq(packers[0](u), packers[1]((z - 1) & 0xF), s, group_size=gs)   # stored z - 1
+    np.testing.assert_array_equal(w1.zeros, w.zeros)
+    a = C.from_awq(packers[2](u), packers[2](z), s, group_size=gs)
+    np.testing.assert_array_equal(_dequant_w4a16(a, gs), _dequant_checkpoint(u, s, z, g))
+
+
+def test_asymmetric_act_order(packers):
+    K, N, gs = 512, 16, 128
+    u, s, z = _inputs(K, N, gs, seed=11, zero=None)
+    g_idx = np.random.default_rng(12).permutation(np.arange(K) // gs)
+    w = C.from_gptq(packers[0](u), packers[1](z), s, g_idx=g_idx, group_size=gs,
+                    checkpoint_format="gptq_v2")
+    got = _dequant_w4a16(w, gs)
+    want = _dequant_checkpoint(u, s, z, g_idx)          # [N, K] in the checkpoint's k order
+    np.testing.assert_array_equal(got, want[:, w.perm])
+
+
+def test_reference_abi_zero_points():
+    """Zero points >= 8 map onto the reference's zp = z - 8; below 8 refused."""
+    K, N, gs = 512, 8, 128
+    rng = np.random.default_rng(5)
+    u = rng.integers(0, 16, (K, N), dtype=np.uint8)
+    s = rng.uniform(0.002, 0.02, (K // gs, N)).astype(np.float16)
+    z = rng.integers(8, 16, (K // gs, N), dtype=np.uint8)
+    w = C.W4A16Weights(C._pack_w4(u), np.ascontiguousarray(s.T), None, np.ascontiguousarray(z.T))
+    packed, scales32, zeros = C.to_reference_abi(w, gs)
+    got = O.dequantize_int4(packed, scales32, zeros, N, K, gs)
+    np.testing.assert_array_equal(got, _dequant_checkpoint(u, s, z, np.arange(K) // gs))
+    low = w._replace(zeros=np.full((N, K // gs), 3, np.uint8))
+    with pytest.raises(ValueError, match="below 8"):
+        C.to_reference_abi(low, gs)
 
 
 @pytest.mark.parametrize("K,gs", [(512, 128), (384, 128), (128, 128)])   # 4, 3 (odd) and 1 group

@@ -230,6 +230,11 @@ class Workload:
         timed: (ok, record).  Workloads without an exchange have none."""
         return True, None
 
+    def step_compute_only(self):
+        """The step without its collective (None: the workload has none); timed
+        apart so the line can name the limiter."""
+        return None
+
     def close(self):
         """Releases what the workload shares with the other ranks."""
 
@@ -456,6 +461,19 @@ class GemmW4A16(Workload):
             self.scaling = "strong"
         self.i = 0
 
+    def step_compute_only(self):
+        if self.col is None:
+            return None
+        x, p, s, _ = self.sets[self.i % self.COPIES]
+        if not hasattr(self, "_local"):
+            self._local = self.torch.empty(self.M, self.n_shard, dtype=self.torch.bfloat16,
+                                           device=self.dev)
+        self.kc_lib.check(self.l.kc_gemm_w4a16(x.data_ptr(), p.data_ptr(), s.data_ptr(),
+                                               self._local.data_ptr(), 0, self.M, self.n_shard,
+                                               self.K, GROUP, self.n_shard, self.s_ptr))
+        self.i += 1
+        return True
+
     def _launch(self, x, p, s, out):
         if self.col is not None:   # fused GEMM + all-gather, then a stream barrier
             # back-to-back steps read nothing in between: the previous step's
@@ -595,7 +613,7 @@ class GemmFP8(Workload):
         self.rp = None
         if world > 1:
             import tp
-            self.rp = tp.RowParallelFP8(M, N, reduce=os.environ.get("KC_TP_REDUCE", "nccl"))
+            self.rp = tp.RowParallelFP8(M, N, reduce=os.environ.get("KC_TP_REDUCE", "overlap"))
             self.scaling = "strong"
         self.i = 0
 
@@ -605,6 +623,16 @@ class GemmFP8(Workload):
         ch = t.randperm(D, device=self.dev, generator=self.gen)[:max(1, round(0.01 * D))]
         x[:, ch] *= 20.0
         return x
+
+    def step_compute_only(self):
+        if self.rp is None:
+            return None
+        qa, sa, qw, sw, out = self.sets[self.i % self.COPIES]
+        self.kc_lib.check(self.l.kc_gemm_fp8(qa.data_ptr(), sa.data_ptr(), qw.data_ptr(),
+                                             sw.data_ptr(), out.data_ptr(), 0, self.M, self.N,
+                                             self.k1 - self.k0, self.N, self.s_ptr))
+        self.i += 1
+        return True
 
     def _launch(self, qa, sa, qw, sw, out):
         if self.rp is not None:   # K-shard partial, then the bf16 sum over NVLink peers
@@ -624,9 +652,12 @@ class GemmFP8(Workload):
     def parallelism(self):
         if self.world == 1:
             return "single GPU"
-        how = ("an NCCL all-reduce on the same stream" if self.rp.reduce == "nccl" else
-               "kc_allreduce_bf16_peer over NVLink peer memory (each GPU reduces 1/N of the "
-               "output in fp32 and writes it to every GPU) between two peer-flag barriers")
+        how = {"nccl": "an NCCL all-reduce on the same stream",
+               "overlap": (f"NCCL all-reduces of {self.rp.chunks} row blocks, each under the next "
+                           f"block's GEMM (GEMM on all but {self.rp.comm_sms} SMs)"),
+               "peer": ("kc_allreduce_bf16_peer over NVLink peer memory (each GPU reduces 1/N of the "
+                        "output in fp32 and writes it to every GPU) between two peer-flag barriers")
+               }[self.rp.reduce]
         return (f"row parallel x{self.world}: K/{self.world} code columns per GPU (scales from "
                 f"full rows), bf16 partials summed by {how}")
 
@@ -812,32 +843,52 @@ class GemvInt4(Workload):
         self.i = 0
 
     def _launch(self, p, s, z):
+        st = ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
         self.kc_lib.check(self.l.kc_gemv_int4_f32(p.data_ptr(), s.data_ptr(), z.data_ptr(),
                                                   self.x.data_ptr(), self.y.data_ptr(), self.R,
-                                                  self.C, GROUP, self.s_ptr))
+                                                  self.C, GROUP, st))
+
+    # One step = one GEMV over each of the COPIES weight copies, replayed as a
+    # CUDA graph: a 9 MB GEMV takes a few microseconds, less than the host
+    # needs to issue one launch through ctypes, so eager steps would time the
+    # host rather than the kernel.
+    launches_per_step = COPIES
 
     def step(self):
-        self._launch(*self.sets[self.i % self.COPIES])
-        self.i += 1
+        torch = self.torch
+        if getattr(self, "graph", None) is None:
+            for args in self.sets:   # one eager pass first
+                self._launch(*args)
+            torch.cuda.synchronize()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
+                for args in self.sets:
+                    self._launch(*args)
+            torch.cuda.synchronize()
+        self.graph.replay()
 
     def work_per_step(self):
         R, C = self.R, self.C
-        return R * C // 2 + R * (C // GROUP) * 4 + R * (C // GROUP // 2) + C * 4 + R * 4
+        return self.COPIES * (R * C // 2 + R * (C // GROUP) * 4 + R * (C // GROUP // 2) + C * 4 + R * 4)
 
     def config(self):
         return {"workload": self.workload_id, "rows": self.R, "cols": self.C,
                 "group_size": GROUP, "bytes_per_step": self.work_per_step(),
+                "launch": f"{self.COPIES} GEMVs per step (one per weight copy), replayed as one CUDA graph",
+                "e2e": "per GEMV: x in from pinned host memory, the launch, y out (no graph)",
                 "l2": f"{self.COPIES} rotating weight copies = 288 MB (larger than L2)"}
 
     def e2e_prepare(self):
         self.h_x = self.x.cpu().pin_memory()
         self.h_y = self.torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
-        return self.h_x.numel() * 4, self.h_y.numel() * 4
+        return self.COPIES * self.h_x.numel() * 4, self.COPIES * self.h_y.numel() * 4
 
     def e2e_step(self):
-        self.x.copy_(self.h_x, non_blocking=True)
-        self.step()
-        self.h_y.copy_(self.y, non_blocking=True)
+        # the reference ABI's use: every GEMV with its own copies in and out
+        for args in self.sets:
+            self.x.copy_(self.h_x, non_blocking=True)
+            self._launch(*args)
+            self.h_y.copy_(self.y, non_blocking=True)
 
     @classmethod
     def _cpu(cls):
@@ -1097,6 +1148,22 @@ def run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, lo
     per_gpu = work / (ms_step * 1e-3) * sc
     value = world * per_gpu
 
+    # ---- the step without its collective (sharded GEMMs): names the limiter
+    compute_only_ms = None
+    if wl.step_compute_only() is not None:
+        for _ in range(2):
+            wl.step_compute_only()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(args.steps):
+            wl.step_compute_only()
+        c1.record(stream)
+        torch.cuda.synchronize()
+        compute_only_ms = _max_over_ranks(torch, dist, world, dev, [c0.elapsed_time(c1) / args.steps])[0]
+
     # ---- e2e: host buffers through the C ABI, copies inside the timed region
     e2e = None
     if not args.no_e2e:
@@ -1146,6 +1213,9 @@ def run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, lo
         cfg["parallelism"] = wl.parallelism()
         if gate is not None:
             cfg["gate"] = gate
+        if compute_only_ms is not None:
+            cfg["split_ms"] = {"step": round(ms_step, 4), "compute_only": round(compute_only_ms, 4),
+                               "collective_exposed": round(ms_step - compute_only_ms, 4)}
         line = {
             "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),

@@ -285,6 +285,13 @@ KC_API int kc_smoothquant_scale(const float* in, const float* smooth, float* out
  * N % 8 == 0, ldc % 8 == 0 and 16-byte aligned codes, sw and out. */
 KC_API int kc_gemm_fp8(const int8_t* a_codes, const float* sa, const int8_t* w_codes, const float* sw,
                        void* out, int out_f32, int M, int N, int K, int ldc, cudaStream_t stream);
+/* kc_gemm_fp8 on at most max_ctas SMs (<= 0: all): the GEMM is persistent,
+ * one CTA per SM, so a collective queued beside it on another stream (the
+ * row-parallel all-reduce of the previous row block) only runs concurrently
+ * if SMs are left free for it. */
+KC_API int kc_gemm_fp8_ctas(const int8_t* a_codes, const float* sa, const int8_t* w_codes,
+                            const float* sw, void* out, int out_f32, int M, int N, int K, int ldc,
+                            int max_ctas, cudaStream_t stream);
 
 /* W4A16 GEMM (prefill) on the tcgen05 tensor cores:
  * out[m, n] = sum_k x[m, k] * w[n, k] with w[n, k] = bf16((u - 8) * s[n, k / gs]),

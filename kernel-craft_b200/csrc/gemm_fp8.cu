@@ -228,8 +228,9 @@ KC_DEFINE_STATUS_READER(gemm_fp8)
 
 extern "C" {
 
-int kc_gemm_fp8(const int8_t* a_codes, const float* sa, const int8_t* w_codes, const float* sw,
-                void* out, int out_f32, int M, int N, int K, int ldc, cudaStream_t stream) {
+int kc_gemm_fp8_ctas(const int8_t* a_codes, const float* sa, const int8_t* w_codes, const float* sw,
+                     void* out, int out_f32, int M, int N, int K, int ldc, int max_ctas,
+                     cudaStream_t stream) {
     KC_REQUIRE(a_codes && sa && w_codes && sw && out, KC_ERR_INVALID_ARG, "null pointer argument");
     KC_REQUIRE(M >= 0 && N >= 0 && K >= 0, KC_ERR_INVALID_ARG, "negative size");
     if (M == 0 || N == 0) return KC_OK;
@@ -261,9 +262,15 @@ int kc_gemm_fp8(const int8_t* a_codes, const float* sa, const int8_t* w_codes, c
                                      (int)smem),
                 "gemm_fp8 shared-memory attribute");
     const int tiles = P.tiles_m * P.tiles_n;
-    const int grid = std::min(tiles, kc::sm_count());
+    const int ctas = max_ctas > 0 ? std::min(max_ctas, kc::sm_count()) : kc::sm_count();
+    const int grid = std::min(tiles, ctas);
     gemm_fp8_kernel<<<grid, kThreads, smem, stream>>>(P);
     return kc::check_launch("gemm_fp8");
+}
+
+int kc_gemm_fp8(const int8_t* a_codes, const float* sa, const int8_t* w_codes, const float* sw,
+                void* out, int out_f32, int M, int N, int K, int ldc, cudaStream_t stream) {
+    return kc_gemm_fp8_ctas(a_codes, sa, w_codes, sw, out, out_f32, M, N, K, ldc, 0, stream);
 }
 
 }  // extern "C"

@@ -98,6 +98,7 @@ _PROTOS = [
     ("kc_smoothquant_scale", ci, [vp, vp, vp, ci, ci, vp]),
     ("kc_sgemm_nt", ci, [vp, vp, vp, ci, ci, ci, vp]),
     ("kc_gemm_fp8", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, vp]),
+    ("kc_gemm_fp8_ctas", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16_act", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16_zp", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, vp]),

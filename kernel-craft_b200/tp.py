@@ -293,9 +293,11 @@ class RowParallelFP8:
     output), with a peer-memory barrier before and after the reduction.
     Returns this rank's [M, N] bf16 output buffer (the same on every rank)."""
 
-    def __init__(self, M: int, N: int, group=None, reduce: str = "peer"):
-        if reduce not in ("peer", "nccl"):
-            raise ValueError("reduce must be 'peer' or 'nccl'")
+    def __init__(self, M: int, N: int, group=None, reduce: str = "peer", chunks: int = 4,
+                 comm_sms: int = 16):
+        if reduce not in ("peer", "nccl", "overlap"):
+            raise ValueError("reduce must be 'peer', 'nccl' or 'overlap'")
+        self.chunks, self.comm_sms = chunks, comm_sms
         self.reduce = reduce
         self.group = group
         self.world = dist.get_world_size(group)
@@ -320,6 +322,9 @@ class RowParallelFP8:
         l = lib()
         if self.reduce == "nccl":   # GEMM into the local output, NCCL sums in place
             return row_parallel_fp8(a_codes_shard, sa, w_codes_shard, sw, self.out, self.group)
+        if self.reduce == "overlap":   # row blocks: block i's all-reduce under block i+1's GEMM
+            return row_parallel_fp8_overlap(a_codes_shard, sa, w_codes_shard, sw, self.out,
+                                            self.chunks, self.comm_sms, self.group)
         if entry_barrier:
             self.barrier()
         check(l.kc_gemm_fp8(ctypes.c_void_p(a_codes_shard.data_ptr()), ctypes.c_void_p(sa.data_ptr()),
@@ -353,6 +358,40 @@ def row_parallel_fp8(a_codes_shard: torch.Tensor, sa: torch.Tensor, w_codes_shar
                             ctypes.c_void_p(w_codes_shard.data_ptr()), ctypes.c_void_p(sw.data_ptr()),
                             ctypes.c_void_p(out.data_ptr()), 0, M, N, Kr, out.stride(0), _stream()))
     dist.all_reduce(out, group=comm_group)
+    return out
+
+
+def row_parallel_fp8_overlap(a_codes_shard: torch.Tensor, sa: torch.Tensor,
+                             w_codes_shard: torch.Tensor, sw: torch.Tensor, out: torch.Tensor,
+                             chunks: int = 4, comm_sms: int = 16, comm_group=None) -> torch.Tensor:
+    """row_parallel_fp8 with the reduction overlapped: the M rows run as
+    `chunks` GEMMs, and each finished row block's bf16 partial is summed by an
+    NCCL all-reduce (on NCCL's own stream, ordered after that block's GEMM)
+    while the next block's GEMM computes.  The GEMMs run on all but comm_sms
+    SMs, which stay free for the collective; the current stream waits for
+    every all-reduce before the call returns.  Same result as
+    row_parallel_fp8, block by block."""
+    M, Kr = a_codes_shard.shape
+    N = w_codes_shard.shape[0]
+    check_row_parallel_fp8(M, N, a_codes_shard, sa, w_codes_shard, sw)
+    if tuple(out.shape) != (M, N) or out.dtype != torch.bfloat16 or not out.is_contiguous() or not out.is_cuda:
+        raise ValueError(f"out: expected a contiguous CUDA bf16 [{M}, {N}] tensor")
+    chunks = max(1, min(chunks, (M + 127) // 128))
+    rows = -(-M // chunks)
+    rows = -(-rows // 128) * 128                # whole 128-row tiles per block
+    ctas = max(1, torch.cuda.get_device_properties(out.device).multi_processor_count - comm_sms)
+    works = []
+    for m0 in range(0, M, rows):
+        mc = min(rows, M - m0)
+        a = a_codes_shard[m0:m0 + mc]
+        o = out[m0:m0 + mc]
+        check(lib().kc_gemm_fp8_ctas(ctypes.c_void_p(a.data_ptr()), ctypes.c_void_p(sa[m0:].data_ptr()),
+                                     ctypes.c_void_p(w_codes_shard.data_ptr()),
+                                     ctypes.c_void_p(sw.data_ptr()), ctypes.c_void_p(o.data_ptr()), 0,
+                                     mc, N, Kr, N, ctas, _stream()))
+        works.append(dist.all_reduce(o, group=comm_group, async_op=True))
+    for w in works:
+        w.wait()
     return out
 
 

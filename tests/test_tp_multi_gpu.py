@@ -4,7 +4,8 @@ Column parallel: the fused GEMM + all-gather (kc_gemm_w4a16_allgather) must
 give every rank the single-GPU kc_gemm_w4a16 result of the full problem bit
 for bit (each output tile is computed by one rank with the same arithmetic and
 stored, unchanged, into every rank's buffer).  Row parallel: the K-sharded FP8
-GEMM + bf16 sum -- by NCCL all-reduce and by the peer-memory kernel
+GEMM + bf16 sum -- by NCCL all-reduce (also row block by row block, each
+block's all-reduce overlapping the next block's GEMM) and by the peer-memory kernel
 kc_allreduce_bf16_peer -- against the single-GPU FP8 GEMM, normwise <= 1e-2
 (bf16 partials are rounded before the sum); the peer sum is identical on
 every rank.  MLP block (tp.MLPBlockW4A16, the reference's col-parallel ->
@@ -74,6 +75,11 @@ def _rank_main(rank, world, port, out_dir):
         tp.row_parallel_fp8(qa_s, sa, qw_s, sw, out)
         torch.cuda.synchronize()
         row_err = float((out.float() - ref).abs().max() / ref.abs().max())
+        # the overlapped form: row blocks whose all-reduce runs under the next block's GEMM
+        out_ov = torch.empty(M2, N2, dtype=torch.bfloat16, device="cuda")
+        tp.row_parallel_fp8_overlap(qa_s, sa, qw_s, sw, out_ov, chunks=2)
+        torch.cuda.synchronize()
+        row_err = max(row_err, float((out_ov.float() - ref).abs().max() / ref.abs().max()))
         rp = tp.RowParallelFP8(M2, N2)
         y2 = rp(qa_s, sa, qw_s, sw)
         torch.cuda.synchronize()

@@ -1294,8 +1294,55 @@ def measure_peak(kind: str, seconds: float, reps: int) -> dict:
             "sustained_launches": count, "clocks": clocks, "torch": torch.__version__}
 
 
+def tc_calibration() -> None:
+    """One launch each of cuBLAS bf16 8192^3 (torch.matmul), torch._scaled_mm
+    fp8 8192^3 and the library's two tcgen05 GEMMs at configs 3 and 4, inside a
+    cudaProfilerStart/Stop window (ncu --profile-from-start off): the same
+    tensor-pipe counters on a library GEMM next to ours."""
+    import torch
+    from kc_lib import check, lib
+    l = lib()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    n = 8192
+    a = torch.randn(n, n, device=dev, generator=g).bfloat16()
+    b = torch.randn(n, n, device=dev, generator=g).bfloat16()
+    a8, b8 = a.float().to(torch.float8_e4m3fn), b.float().to(torch.float8_e4m3fn).t()
+    one = torch.ones((), device=dev)
+    M, N, K = GemmW4A16.M, GemmW4A16.N, GemmW4A16.K
+    x = torch.randn(M, K, device=dev, generator=g).bfloat16()
+    p = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
+    sc = (torch.rand(N, K // GROUP, device=dev, generator=g) * 0.018 + 0.002).half()
+    o = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    M4, N4, K4 = GemmFP8.M, GemmFP8.N, GemmFP8.K
+    qa = torch.randint(-100, 100, (M4, K4), dtype=torch.int8, device=dev, generator=g)
+    qw = torch.randint(-100, 100, (N4, K4), dtype=torch.int8, device=dev, generator=g)
+    sa, sw = torch.rand(M4, device=dev, generator=g), torch.rand(N4, device=dev, generator=g)
+    o4 = torch.empty(M4, N4, dtype=torch.bfloat16, device=dev)
+
+    def run():
+        torch.matmul(a, b)
+        torch._scaled_mm(a8, b8, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        check(l.kc_gemm_w4a16(x.data_ptr(), p.data_ptr(), sc.data_ptr(), o.data_ptr(), 0, M, N, K,
+                              GROUP, N, st))
+        check(l.kc_gemm_fp8(qa.data_ptr(), sa.data_ptr(), qw.data_ptr(), sw.data_ptr(), o4.data_ptr(),
+                            0, M4, N4, K4, N4, st))
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    run()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    print(json.dumps({"tc_calibration": "ok"}), flush=True)
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--tc-calibration", action="store_true",
+                    help="run cuBLAS bf16/fp8 and the two tcgen05 GEMMs once in a profiler window")
     ap.add_argument("--peak", choices=["bf16", "fp8"], default=None,
                     help="measure a library GEMM's dense tensor-core peak instead (one JSON line)")
     ap.add_argument("--peak-seconds", type=float, default=4.0)
@@ -1317,6 +1364,9 @@ def main(argv=None) -> int:
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
 
+    if args.tc_calibration:
+        tc_calibration()
+        return 0
     if args.peak is not None:
         print(json.dumps(measure_peak(args.peak, args.peak_seconds, args.peak_reps)), flush=True)
         return 0

@@ -104,7 +104,18 @@ __device__ __forceinline__ float nib_f32(uint32_t w, int e) {  // 2^23 + 16^e * 
     return __uint_as_float((w & (0xFu << (4 * e))) ^ (0x4B000000u | (8u << (4 * e))));
 }
 
-__device__ __forceinline__ float chunk_dot(const uint4& v, const float4* xv, float z8) {
+// xa: this chunk's 32 activations in shared memory (8 float4, 32 bytes per
+// q-step: two 16-byte halves)
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t xa_base(uint32_t x0, int q) { return x0 + 32u * (uint32_t)q; }
+
+__device__ __forceinline__ float chunk_dot(const uint4& v, uint32_t x0, float z8) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     float k[5], t[5];
 #pragma unroll
@@ -114,7 +125,7 @@ __device__ __forceinline__ float chunk_dot(const uint4& v, const float4* xv, flo
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        const float4 xa = __ldg(xv + 2 * q), xb = __ldg(xv + 2 * q + 1);
+        const float4 xa = lds_f4(xa_base(x0, q)), xb = lds_f4(xa_base(x0, q) + 16);
         const float xe[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
         const uint32_t h = w[q] >> 20;
 #pragma unroll
@@ -128,6 +139,13 @@ __device__ __forceinline__ float chunk_dot(const uint4& v, const float4* xv, flo
     return c;
 }
 
+// x lives in shared memory for the whole CTA: lane l's chunk j needs the 32
+// activations 32j .. 32j + 31, so neighbouring lanes read 128 bytes apart --
+// from global memory every such load touches 32 cache lines.  A 16-byte pad
+// after every 128 bytes (chunk j at byte 144 j) spreads eight lanes' 16-byte
+// reads over all 32 banks.
+__host__ __device__ constexpr size_t xs_bytes(int cols) { return (size_t)cols / 32 * 144; }
+
 __global__ void __launch_bounds__(256, 4) gemv_int4_f32_vec(const uint8_t* __restrict__ packed,
                                                             const float* __restrict__ scales,
                                                             const uint8_t* __restrict__ zeros,
@@ -135,38 +153,48 @@ __global__ void __launch_bounds__(256, 4) gemv_int4_f32_vec(const uint8_t* __res
                                                             float* __restrict__ y, int rows, int cols,
                                                             int gs, int gs_shift) {
     constexpr int kU = 4;
+    extern __shared__ __align__(16) uint8_t xs_raw[];
     const int lane = threadIdx.x & 31;
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (r >= rows) return;
+    const bool live = r < rows;
     const int sc = cols / gs, cpr = cols / 32, zc = sc / 2;  // the reference's floor zero stride
-    const uint8_t* p = packed + (long)r * (cols / 2);
-    const float* srow = scales + (long)r * sc;
-    const uint8_t* zrow = zeros + (long)r * zc;
-    float acc = 0.f;
-    for (int jb = lane; jb < cpr; jb += 32 * kU) {
-        // every global load of the kU chunks (weights, scales, zero points)
-        // is in flight before the first chunk is computed
-        uint4 v[kU];
-        float s[kU];
-        uint32_t zb[kU];
-        int g[kU];
+    const uint8_t* p = packed + (long)min(r, rows - 1) * (cols / 2);
+    const float* srow = scales + (long)min(r, rows - 1) * sc;
+    const uint8_t* zrow = zeros + (long)min(r, rows - 1) * zc;
+    // the first kU chunks' weights, scales and zero points are requested
+    // before the activations are staged
+    uint4 v[kU];
+    float s[kU];
+    uint32_t zb[kU];
+    int g[kU];
+    auto issue = [&](int jb) {
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             const int j = jb + 32 * u;
-            if (j < cpr) {
+            if (live && j < cpr) {
                 g[u] = gs_shift >= 0 ? (32 * j) >> gs_shift : (32 * j) / gs;
                 v[u] = kc_ldg_stream(p + 16 * j);
                 s[u] = __ldg(srow + g[u]);
                 zb[u] = __ldg(zrow + (g[u] >> 1));
             }
         }
+    };
+    issue(lane);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int i = threadIdx.x; i < cols / 4; i += blockDim.x)
+        *reinterpret_cast<float4*>(xs_raw + 16 * i + 16 * (i >> 3)) = __ldg(x4 + i);
+    __syncthreads();
+    if (!live) return;
+    const uint32_t xs0 = (uint32_t)__cvta_generic_to_shared(xs_raw);
+    float acc = 0.f;
+    for (int jb = lane; jb < cpr; jb += 32 * kU) {
+        if (jb != lane) issue(jb);
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             const int j = jb + 32 * u;
             if (j >= cpr) break;
             const uint32_t z = (g[u] & 1) ? (zb[u] >> 4) : (zb[u] & 15u);
-            acc = fmaf(s[u], chunk_dot(v[u], reinterpret_cast<const float4*>(x + 32 * j), (float)(8 + z)),
-                       acc);
+            acc = fmaf(s[u], chunk_dot(v[u], xs0 + 144u * (uint32_t)j, (float)(8 + z)), acc);
         }
     }
     acc = kc_warp_sum(acc);
@@ -307,8 +335,10 @@ int kc_gemv_int4_f32(const uint8_t* packed, const float* scales, const uint8_t* 
     if (st) return st;
     KC_REQUIRE(x != nullptr, KC_ERR_INVALID_ARG, "null x");
     if (rows == 0) return KC_OK;
+    // the vector path stages x in shared memory: up to 48 KB (cols <= 10922
+    // rounded to chunks) without an opt-in attribute
     const bool vec = (cols % 32 == 0) && (gs % 32 == 0) && kc::aligned(packed, 16) &&
-                     kc::aligned(x, 16);
+                     kc::aligned(x, 16) && xs_bytes(cols) <= 48 * 1024;
     if (vec) {
         // 8 rows per CTA, one CTA per 8 rows (no grid-stride loop)
         const long ctas = ((long)rows + 7) / 8;
@@ -316,8 +346,8 @@ int kc_gemv_int4_f32(const uint8_t* packed, const float* scales, const uint8_t* 
         int gs_shift = -1;
         for (int b = 0; b < 31; ++b)
             if (gs == (1 << b)) gs_shift = b;
-        gemv_int4_f32_vec<<<(unsigned)ctas, 256, 0, stream>>>(packed, scales, zeros, x, y, rows, cols, gs,
-                                                             gs_shift);
+        gemv_int4_f32_vec<<<(unsigned)ctas, 256, xs_bytes(cols), stream>>>(packed, scales, zeros, x, y,
+                                                                           rows, cols, gs, gs_shift);
         return kc::check_launch("gemv_int4_f32");
     }
     const int grid = grid_for(((long)rows + 7) / 8, 256);

@@ -613,7 +613,17 @@ class GemmFP8(Workload):
         self.rp = None
         if world > 1:
             import tp
-            self.rp = tp.RowParallelFP8(M, N, reduce=os.environ.get("KC_TP_REDUCE", "overlap"))
+            # measured on 2 B200s: an NCCL all-reduce after the whole GEMM beats
+            # the in-switch sum there (it moves 1.5x the bytes of a ring at
+            # 2 ranks, (1 + 1/N)x the output at N) and beats splitting the GEMM
+            # into blocks; from 4 ranks on the in-switch sum moves fewer bytes
+            reduce = os.environ.get("KC_TP_REDUCE", "nccl" if world == 2 else "nvls")
+            kw = dict(chunks=int(os.environ.get("KC_TP_CHUNKS", "4")),
+                      comm_sms=int(os.environ.get("KC_TP_COMM_SMS", "16")))
+            try:
+                self.rp = tp.RowParallelFP8(M, N, reduce=reduce, **kw)
+            except RuntimeError:        # no NVLink multicast: NCCL sums under the GEMMs
+                self.rp = tp.RowParallelFP8(M, N, reduce="overlap", **kw)
             self.scaling = "strong"
         self.i = 0
 
@@ -656,7 +666,11 @@ class GemmFP8(Workload):
                "overlap": (f"NCCL all-reduces of {self.rp.chunks} row blocks, each under the next "
                            f"block's GEMM (GEMM on all but {self.rp.comm_sms} SMs)"),
                "peer": ("kc_allreduce_bf16_peer over NVLink peer memory (each GPU reduces 1/N of the "
-                        "output in fp32 and writes it to every GPU) between two peer-flag barriers")
+                        "output in fp32 and writes it to every GPU) between two peer-flag barriers"),
+               "nvls": (f"the NVSwitch in place (kc_allreduce_bf16_nvls: multimem.ld_reduce with fp32 "
+                        f"accumulation + multimem.st on a symmetric buffer) for {self.rp.chunks} row "
+                        f"blocks, each behind a peer-flag barrier and under the next block's GEMM "
+                        f"(GEMM on all but {self.rp.comm_sms} SMs)")
                }[self.rp.reduce]
         return (f"row parallel x{self.world}: K/{self.world} code columns per GPU (scales from "
                 f"full rows), bf16 partials summed by {how}")
@@ -1339,10 +1353,59 @@ def tc_calibration() -> None:
     print(json.dumps({"tc_calibration": "ok"}), flush=True)
 
 
+def stream_floor(reps: int = 20) -> dict:
+    """The floor the config-0 GEMV is measured against: the library's plain
+    streaming-read kernel (kc_selftest_stream_read, same CTA shape and loads in
+    flight as gemv_int4_f32_vec) over the GEMV's bytes per launch, 32 rotating
+    buffers replayed as one CUDA graph exactly like the GemvInt4 step, and the
+    same graph of 32 empty launches (the launch floor)."""
+    import torch
+    from kc_lib import check, lib
+    l = lib()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    R, C = GemvInt4.R, GemvInt4.C
+    nbytes = R * C // 2 + R * (C // GROUP) * 4 + R * (C // GROUP // 2) + C * 4 + R * 4
+    bufs = [torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=dev)
+            for _ in range(GemvInt4.COPIES)]
+    sink = torch.zeros(4, dtype=torch.int32, device=dev)
+    out = {"bytes_per_launch": nbytes, "launches_per_graph": GemvInt4.COPIES}
+    for label, size in (("read", nbytes), ("empty", 0)):
+        def launches():
+            st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for buf in bufs:
+                check(l.kc_selftest_stream_read(buf.data_ptr(), size, 0x9E3779B9, sink.data_ptr(), st))
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            launches()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
+                launches()
+            for _ in range(5):
+                g.replay()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                g.replay()
+                e1.record(s)
+                e1.synchronize()
+                times.append(e0.elapsed_time(e1) * 1e3 / GemvInt4.COPIES)
+        us = float(np.median(times))
+        out[f"{label}_us_per_launch"] = round(us, 3)
+        if size:
+            out["read_gbs"] = round(nbytes / us / 1e3, 1)
+        del g
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--tc-calibration", action="store_true",
                     help="run cuBLAS bf16/fp8 and the two tcgen05 GEMMs once in a profiler window")
+    ap.add_argument("--stream-floor", action="store_true",
+                    help="time a plain streaming read of the config-0 GEMV's bytes per launch")
     ap.add_argument("--peak", choices=["bf16", "fp8"], default=None,
                     help="measure a library GEMM's dense tensor-core peak instead (one JSON line)")
     ap.add_argument("--peak-seconds", type=float, default=4.0)
@@ -1366,6 +1429,9 @@ def main(argv=None) -> int:
 
     if args.tc_calibration:
         tc_calibration()
+        return 0
+    if args.stream_floor:
+        print(json.dumps({"stream_floor": stream_floor()}), flush=True)
         return 0
     if args.peak is not None:
         print(json.dumps(measure_peak(args.peak, args.peak_seconds, args.peak_reps)), flush=True)

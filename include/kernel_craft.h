@@ -63,6 +63,14 @@ KC_API int kc_get_device_status(void);
  * kc_get_device_status() and writes the milliseconds waited to
  * *waited_ms_device (device int).  The context stays usable. */
 KC_API int kc_selftest_bounded_wait(uint64_t timeout_ns, int* waited_ms_device, cudaStream_t stream);
+/* Measurement hook: one pass of 16-byte streaming loads over `bytes` bytes at
+ * `src` (16-byte aligned, bytes a multiple of 16) with the launch shape of the
+ * reference-ABI GEMV (256-thread CTAs, four loads in flight per thread), the
+ * floor that GEMV is measured against.  Nothing is written unless the XOR of
+ * all words equals `sentinel`, in which case one word goes to *sink_device.
+ * bytes == 0 launches one empty CTA (the launch floor). */
+KC_API int kc_selftest_stream_read(const void* src, size_t bytes, uint32_t sentinel,
+                                   uint32_t* sink_device, cudaStream_t stream);
 
 /* ======================================================================= */
 /* Part 1: reference launcher ABI (drop-in)                                 */
@@ -362,6 +370,20 @@ KC_API int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed
  * count % (8 * nranks) == 0, 16-byte aligned buffers, nranks <= KC_MAX_RANKS. */
 KC_API int kc_allreduce_bf16_peer(const void* const* partials, void* const* outs, int nranks,
                                   int rank, long count, cudaStream_t stream);
+
+/* bf16 sum all-reduce in place through NVLink SHARP (the switch's multicast
+ * and in-switch reduction; no reference counterpart).  mc: the multicast
+ * address of a buffer of `count` bf16 bound on every rank (e.g. a symmetric
+ * allocation's multicast pointer).  This rank reduces the rank-th 1/nranks
+ * slice (multimem.ld_reduce, fp32 accumulation in the switch) and writes the
+ * sum into every rank's copy (multimem.st).  Synchronization as for
+ * kc_allreduce_bf16_peer: every rank's data must be complete before any rank
+ * launches (kc_peer_barrier), the result is complete once every rank's launch
+ * has finished; after a barrier timeout it writes NaN.  max_ctas > 0 caps the
+ * grid (leaves SMs to a concurrent GEMM).  count % (8 * nranks) == 0, mc
+ * 16-byte aligned. */
+KC_API int kc_allreduce_bf16_nvls(void* mc, int nranks, int rank, long count, int max_ctas,
+                                  cudaStream_t stream);
 
 /* Stream-ordered barrier of the ranks of one node over peer memory (no
  * reference counterpart).  flags[r]: rank r's array of KC_MAX_RANKS ints

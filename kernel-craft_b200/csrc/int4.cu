@@ -86,22 +86,57 @@ __global__ void dequant_int4_f32_vec(const uint8_t* __restrict__ packed,
 
 // fp32 GEMV over 16-byte chunks (32 weights of one group each), one warp per
 // row: a lane takes chunks lane, lane + 32, ... and issues the loads of kU of
-// them before it computes any (kU * 16 bytes in flight per lane; a grid of
-// rows / 8 CTAs of eight warps fills every SM three or four times over).
+// them before it computes any (kU * 16 bytes in flight per lane).  One CTA of
+// 32 warps per SM, rows dealt round-robin over the CTAs, so each SM holds at
+// most ceil(rows / 148) rows (28 at 4096) and stages the activations once.
 //
-// Dequantization without conversion instructions: a nibble u at bits 4e of a
-// word, for e <= 4, becomes the exact float 2^23 + 16^e * (u ^ 8) by one
-// LOP3 ((w & 0xF << 4e) ^ (0x4B000000 | 8 << 4e): the float's mantissa holds
-// the flipped nibble in place, its exponent is 2^23); subtracting the exact
-// constant 2^23 + (8 + z) * 16^e leaves (sx4(u) - z) * 16^e, the reference's
-// integer weight (quant_int4.cu:99-104) times 16^e, and one FMA accumulates it
-// against x in the accumulator of that power of 16.  Nibbles 5..7 come from
-// the word shifted right by 20 the same way.  Per chunk the five accumulators
-// combine as sum_e t_e * 16^-e (exact scalings) and the group scale
-// multiplies the result: the chunk's sum, then its scale, where the
-// reference scales every weight first -- fp32 GEMV parity is normwise.
-__device__ __forceinline__ float nib_f32(uint32_t w, int e) {  // 2^23 + 16^e * (u ^ 8)
-    return __uint_as_float((w & (0xFu << (4 * e))) ^ (0x4B000000u | (8u << (4 * e))));
+// Dequantization without conversion instructions: the word is XOR-ed with
+// 0x88888888 once (each nibble u becomes u' = u ^ 8 = sx4(u) + 8), then a
+// nibble at bits 4e, for e <= 4, becomes the exact float 2^23 + 16^e * u' by
+// one LOP3 ((w' & 0xF << 4e) | 0x4B000000: the float's mantissa holds the
+// nibble in place, its exponent is 2^23); subtracting 2^23 (exact) leaves
+// 16^e * u', and one FMA accumulates it against x.  Nibbles 5..7 come from
+// the word shifted right by 20 the same way.  The subtractions and FMAs run
+// as packed f32x2 pairs (positions p, p + 1 of a word: add.rn.f32x2 /
+// fma.rn.f32x2, sm_100) into eight accumulators, one per position; positions
+// p and p + 5 share the power 16^p, and the five sums combine as
+// sum_e t_e * 16^-e (exact scalings) into sum u' x over the chunk.  The
+// reference's weight (quant_int4.cu:99-104) is sx4(u) - z = u' - (8 + z), so
+// the chunk's dot product is sum u' x - (8 + z) * X, X the chunk's activation
+// sum (computed once per CTA while x is staged); then the group scale
+// multiplies it: the chunk's sum, then its scale, where the reference scales
+// every weight first -- fp32 GEMV parity is normwise.
+//
+// expo = 0x4B000000 arrives as a kernel argument, so it sits in a register and
+// each nibble costs one LOP3 with the mask as its only immediate (with both
+// constants immediate the compiler splits the operation in two).
+template <int E>
+__device__ __forceinline__ uint32_t nib_bits(uint32_t w, uint32_t expo) {  // 2^23 + 16^E * u'
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(w), "n"(0xFu << (4 * E)), "r"(expo));  // (a & b) | c
+    return d;
+}
+
+__device__ __forceinline__ uint64_t f2pack(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+    return f2pack(__float_as_uint(lo), __float_as_uint(hi));
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
 }
 
 // xa: this chunk's 32 activations in shared memory (8 float4, 32 bytes per
@@ -115,28 +150,35 @@ __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
 
 __device__ __forceinline__ uint32_t xa_base(uint32_t x0, int q) { return x0 + 32u * (uint32_t)q; }
 
-__device__ __forceinline__ float chunk_dot(const uint4& v, uint32_t x0, float z8) {
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    float k[5], t[5];
-#pragma unroll
-    for (int e = 0; e < 5; ++e) {
-        k[e] = fmaf(z8, (float)(1 << (4 * e)), 8388608.f);
-        t[e] = 0.f;
-    }
+// sum over the chunk of u' * x, u' = (nibble ^ 8) in 0..15; nexp2 holds the
+// pair (-2^23, -2^23)
+__device__ __forceinline__ float chunk_dot(const uint4& v, uint32_t x0, uint64_t nexp2, uint32_t expo) {
+    const uint32_t w[4] = {v.x ^ 0x88888888u, v.y ^ 0x88888888u, v.z ^ 0x88888888u, v.w ^ 0x88888888u};
+    uint64_t a[4] = {0, 0, 0, 0};   // accumulator pairs (p, p + 1), p = 0, 2, 4, 6
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         const float4 xa = lds_f4(xa_base(x0, q)), xb = lds_f4(xa_base(x0, q) + 16);
-        const float xe[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
         const uint32_t h = w[q] >> 20;
-#pragma unroll
-        for (int e = 0; e < 5; ++e) t[e] = fmaf(nib_f32(w[q], e) - k[e], xe[e], t[e]);
-#pragma unroll
-        for (int e = 0; e < 3; ++e) t[e] = fmaf(nib_f32(h, e) - k[e], xe[5 + e], t[e]);
+        const uint64_t n01 = f2pack(nib_bits<0>(w[q], expo), nib_bits<1>(w[q], expo));
+        const uint64_t n23 = f2pack(nib_bits<2>(w[q], expo), nib_bits<3>(w[q], expo));
+        const uint64_t n45 = f2pack(nib_bits<4>(w[q], expo), nib_bits<0>(h, expo));
+        const uint64_t n67 = f2pack(nib_bits<1>(h, expo), nib_bits<2>(h, expo));
+        a[0] = f2fma(f2add(n01, nexp2), f2pack(xa.x, xa.y), a[0]);
+        a[1] = f2fma(f2add(n23, nexp2), f2pack(xa.z, xa.w), a[1]);
+        a[2] = f2fma(f2add(n45, nexp2), f2pack(xb.x, xb.y), a[2]);
+        a[3] = f2fma(f2add(n67, nexp2), f2pack(xb.z, xb.w), a[3]);
     }
+    float t[8];
+    f2unpack(a[0], t[0], t[1]);
+    f2unpack(a[1], t[2], t[3]);
+    f2unpack(a[2], t[4], t[5]);
+    f2unpack(a[3], t[6], t[7]);
+    // t_e for e = 0..4: positions e and e + 5 (e < 3)
     float c = t[4];
-#pragma unroll
-    for (int e = 3; e >= 0; --e) c = fmaf(c, 0.0625f, t[e]);
-    return c;
+    c = fmaf(c, 0.0625f, t[3]);
+    c = fmaf(c, 0.0625f, t[2] + t[7]);
+    c = fmaf(c, 0.0625f, t[1] + t[6]);
+    return fmaf(c, 0.0625f, t[0] + t[5]);
 }
 
 // x lives in shared memory for the whole CTA: lane l's chunk j needs the 32
@@ -146,21 +188,40 @@ __device__ __forceinline__ float chunk_dot(const uint4& v, uint32_t x0, float z8
 // reads over all 32 banks.
 __host__ __device__ constexpr size_t xs_bytes(int cols) { return (size_t)cols / 32 * 144; }
 
-__global__ void __launch_bounds__(256, 4) gemv_int4_f32_vec(const uint8_t* __restrict__ packed,
-                                                            const float* __restrict__ scales,
-                                                            const uint8_t* __restrict__ zeros,
-                                                            const float* __restrict__ x,
-                                                            float* __restrict__ y, int rows, int cols,
-                                                            int gs, int gs_shift) {
+__global__ void __launch_bounds__(1024, 1) gemv_int4_f32_vec(const uint8_t* __restrict__ packed,
+                                                             const float* __restrict__ scales,
+                                                             const uint8_t* __restrict__ zeros,
+                                                             const float* __restrict__ x,
+                                                             float* __restrict__ y, int rows, int cols,
+                                                             int gs, int gs_shift, uint32_t expo) {
     constexpr int kU = 4;
     extern __shared__ __align__(16) uint8_t xs_raw[];
     const int lane = threadIdx.x & 31;
-    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    // rows blockIdx + gridDim * (warp + 32 k): every SM holds at most
+    // ceil(rows / gridDim) rows and stages x once
+    const int rstep = gridDim.x * (blockDim.x >> 5);
+    int r = blockIdx.x + gridDim.x * (threadIdx.x >> 5);
     const bool live = r < rows;
     const int sc = cols / gs, cpr = cols / 32, zc = sc / 2;  // the reference's floor zero stride
     const uint8_t* p = packed + (long)min(r, rows - 1) * (cols / 2);
     const float* srow = scales + (long)min(r, rows - 1) * sc;
     const uint8_t* zrow = zeros + (long)min(r, rows - 1) * zc;
+    // Programmatic dependent launch: the next GEMV on the stream may be
+    // scheduled now; it waits (griddepcontrol.wait) before it reads anything.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // While the previous grid drains, pull this warp's first row into L2: its
+    // packed weights (128-byte lines), scales and zero points.  A prefetch
+    // only moves lines into L2, where the previous grid's writes land, so it
+    // is safe whatever that grid wrote; every read below comes after the wait.
+    if (live) {
+        const int wl = (cols / 2 + 127) / 128, sl = (sc * 4 + 127) / 128;
+        for (int i = lane; i < wl + sl + 1; i += 32) {
+            const void* a = i < wl ? (const void*)(p + 128 * i)
+                          : i < wl + sl ? (const void*)(srow + 32 * (i - wl)) : (const void*)zrow;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // the first kU chunks' weights, scales and zero points are requested
     // before the activations are staged
     uint4 v[kU];
@@ -171,7 +232,7 @@ __global__ void __launch_bounds__(256, 4) gemv_int4_f32_vec(const uint8_t* __res
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             const int j = jb + 32 * u;
-            if (live && j < cpr) {
+            if (j < cpr) {
                 g[u] = gs_shift >= 0 ? (32 * j) >> gs_shift : (32 * j) / gs;
                 v[u] = kc_ldg_stream(p + 16 * j);
                 s[u] = __ldg(srow + g[u]);
@@ -179,26 +240,52 @@ __global__ void __launch_bounds__(256, 4) gemv_int4_f32_vec(const uint8_t* __res
             }
         }
     };
-    issue(lane);
+    if (live) issue(lane);
+    // x into shared memory, and each chunk's sum X into the 16-byte pad after
+    // its 128 bytes.  The eight threads of a chunk are eight consecutive lanes
+    // starting at a multiple of 8 (the loop stride is a multiple of 8 and
+    // cols / 4 is one), and they enter an iteration together: the shuffles
+    // stay within those eight.
     const float4* x4 = reinterpret_cast<const float4*>(x);
-    for (int i = threadIdx.x; i < cols / 4; i += blockDim.x)
-        *reinterpret_cast<float4*>(xs_raw + 16 * i + 16 * (i >> 3)) = __ldg(x4 + i);
+    const unsigned oct = 0xFFu << (lane & 24);
+    for (int i = threadIdx.x; i < cols / 4; i += blockDim.x) {
+        const float4 f = __ldg(x4 + i);
+        *reinterpret_cast<float4*>(xs_raw + 16 * i + 16 * (i >> 3)) = f;
+        float t = (f.x + f.y) + (f.z + f.w);
+        t += __shfl_xor_sync(oct, t, 1);
+        t += __shfl_xor_sync(oct, t, 2);
+        t += __shfl_xor_sync(oct, t, 4);
+        if ((i & 7) == 0) *reinterpret_cast<float*>(xs_raw + 144 * (i >> 3) + 128) = t;
+    }
     __syncthreads();
     if (!live) return;
     const uint32_t xs0 = (uint32_t)__cvta_generic_to_shared(xs_raw);
-    float acc = 0.f;
-    for (int jb = lane; jb < cpr; jb += 32 * kU) {
-        if (jb != lane) issue(jb);
+    const uint64_t nexp2 = f2pack(-8388608.f, -8388608.f);
+    while (true) {
+        float acc = 0.f;
+        for (int jb = lane; jb < cpr; jb += 32 * kU) {
+            if (jb != lane) issue(jb);
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int j = jb + 32 * u;
-            if (j >= cpr) break;
-            const uint32_t z = (g[u] & 1) ? (zb[u] >> 4) : (zb[u] & 15u);
-            acc = fmaf(s[u], chunk_dot(v[u], xs0 + 144u * (uint32_t)j, (float)(8 + z)), acc);
+            for (int u = 0; u < kU; ++u) {
+                const int j = jb + 32 * u;
+                if (j >= cpr) break;
+                const uint32_t z = (g[u] & 1) ? (zb[u] >> 4) : (zb[u] & 15u);
+                const uint32_t xj = xs0 + 144u * (uint32_t)j;
+                float xsum;
+                asm volatile("ld.shared.f32 %0, [%1];" : "=f"(xsum) : "r"(xj + 128u));
+                const float d = fmaf(-(float)(8u + z), xsum, chunk_dot(v[u], xj, nexp2, expo));
+                acc = fmaf(s[u], d, acc);
+            }
         }
+        acc = kc_warp_sum(acc);
+        if (lane == 0) y[r] = acc;
+        r += rstep;
+        if (r >= rows) break;
+        p = packed + (long)r * (cols / 2);
+        srow = scales + (long)r * sc;
+        zrow = zeros + (long)r * zc;
+        issue(lane);
     }
-    acc = kc_warp_sum(acc);
-    if (lane == 0) y[r] = acc;
 }
 
 // fp32 GEMV, one warp per row, one packed byte per lane and step: any shape
@@ -340,15 +427,25 @@ int kc_gemv_int4_f32(const uint8_t* packed, const float* scales, const uint8_t* 
     const bool vec = (cols % 32 == 0) && (gs % 32 == 0) && kc::aligned(packed, 16) &&
                      kc::aligned(x, 16) && xs_bytes(cols) <= 48 * 1024;
     if (vec) {
-        // 8 rows per CTA, one CTA per 8 rows (no grid-stride loop)
-        const long ctas = ((long)rows + 7) / 8;
-        KC_REQUIRE(ctas < (1L << 31), KC_ERR_INVALID_ARG, "too many rows");
+        // one 32-warp CTA per SM (fewer for fewer rows), a warp per row
+        const long ctas = std::min<long>(rows, kc::sm_count());
         int gs_shift = -1;
         for (int b = 0; b < 31; ++b)
             if (gs == (1 << b)) gs_shift = b;
-        gemv_int4_f32_vec<<<(unsigned)ctas, 256, xs_bytes(cols), stream>>>(packed, scales, zeros, x, y,
-                                                                           rows, cols, gs, gs_shift);
-        return kc::check_launch("gemv_int4_f32");
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)ctas);
+        cfg.blockDim = dim3(1024);
+        cfg.dynamicSmemBytes = xs_bytes(cols);
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        KC_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_int4_f32_vec, packed, scales, zeros, x, y, rows, cols,
+                                       gs, gs_shift, 0x4B000000u),
+                    "gemv_int4_f32 launch");
+        return KC_OK;
     }
     const int grid = grid_for(((long)rows + 7) / 8, 256);
     gemv_int4_f32_bytes<<<grid, 256, 0, stream>>>(packed, scales, zeros, x, y, rows, cols, gs);

@@ -85,6 +85,42 @@ __global__ void __launch_bounds__(256) peer_allreduce_bf16_kernel(const __grid_c
     }
 }
 
+// NVLink SHARP form: `mc` is the multicast address of a buffer bound on every
+// rank (one physical copy per GPU).  Vectors [begin, end) of 8 bf16 -- this
+// rank's slice -- are read through the switch, which sums the R copies
+// (multimem.ld_reduce, fp32 accumulation), and the sum is written back
+// through the switch into every rank's copy (multimem.st).  Per GPU the
+// switch reads (R-1)/R of the array and writes (R-1)/R of it, once each: the
+// traffic of a single pass, against 2(R-1)/R for the peer form.  Only the
+// reducing rank touches its slice, so the sum can be in place.
+__global__ void __launch_bounds__(256) nvls_allreduce_bf16_kernel(uint4* mc, long begin, long end) {
+    constexpr int U = 4;
+    const bool poison = *reinterpret_cast<volatile int*>(&g_peer_status) != 0;
+    const long stride = (long)gridDim.x * blockDim.x * U;
+    for (long base = begin + (long)blockIdx.x * blockDim.x * U + threadIdx.x; base < end; base += stride) {
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const long i = base + (long)u * blockDim.x;
+            if (i < end)
+                asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(v[u].x), "=r"(v[u].y), "=r"(v[u].z), "=r"(v[u].w)
+                             : "l"(mc + i)
+                             : "memory");
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const long i = base + (long)u * blockDim.x;
+            if (i >= end) break;
+            const uint4 o = poison ? make_uint4(0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u, 0x7FC07FC0u) : v[u];
+            asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};"
+                         ::"l"(mc + i), "r"(o.x), "r"(o.y), "r"(o.z), "r"(o.w)
+                         : "memory");
+        }
+    }
+    __threadfence_system();   // the stores before the barrier that follows the kernel
+}
+
 template <int R>
 void launch_r(const PeerPtrs& p, long begin, long end, cudaStream_t stream) {
     const long vecs = end - begin;
@@ -205,6 +241,25 @@ int kc_allreduce_bf16_peer(const void* const* partials, void* const* outs, int n
         default: launch_r<8>(p, begin, end, stream); break;
     }
     return kc::check_launch("peer_allreduce_bf16");
+}
+
+int kc_allreduce_bf16_nvls(void* mc, int nranks, int rank, long count, int max_ctas,
+                           cudaStream_t stream) {
+    KC_REQUIRE(mc && nranks >= 1 && nranks <= KC_MAX_RANKS && rank >= 0 && rank < nranks,
+               KC_ERR_INVALID_ARG, "rank %d of %d outside 0..%d", rank, nranks, KC_MAX_RANKS - 1);
+    KC_REQUIRE(kc::aligned(mc, 16), KC_ERR_ALIGNMENT, "multicast address not 16-byte aligned");
+    KC_REQUIRE(count >= 0 && count % (8L * nranks) == 0, KC_ERR_INVALID_ARG,
+               "count=%ld must be a multiple of 8 * nranks", count);
+    KC_REQUIRE(max_ctas >= 0, KC_ERR_INVALID_ARG, "max_ctas=%d", max_ctas);
+    if (count == 0) return KC_OK;
+    const long slice = count / 8 / nranks;
+    const long begin = slice * rank, end = begin + slice;
+    long grid = (slice + 4 * 256 - 1) / (4 * 256);
+    grid = std::min(grid, (long)kc::sm_count() * 4);
+    if (max_ctas > 0) grid = std::min(grid, (long)max_ctas);
+    nvls_allreduce_bf16_kernel<<<(unsigned)std::max(1L, grid), 256, 0, stream>>>(static_cast<uint4*>(mc),
+                                                                                 begin, end);
+    return kc::check_launch("nvls_allreduce_bf16");
 }
 
 }  // extern "C"

@@ -54,6 +54,7 @@ _PROTOS = [
     ("kc_version", ctypes.c_char_p, []),
     ("kc_get_device_status", ci, []),
     ("kc_selftest_bounded_wait", ci, [ctypes.c_uint64, vp, vp]),
+    ("kc_selftest_stream_read", ci, [vp, ctypes.c_size_t, ctypes.c_uint32, vp, vp]),
     # reference ABI
     ("launch_dequantize_int4", None, [vp, vp, vp, vp, ci, ci, ci, vp]),
     ("launch_gemv_int4", None, [vp, vp, vp, vp, vp, ci, ci, ci, vp]),
@@ -104,6 +105,7 @@ _PROTOS = [
     ("kc_gemm_w4a16_zp", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_gemm_w4a16_allgather", ci, [vp, vp, vp, ctypes.POINTER(vp), ci, ci, ci, ci, ci, ci, vp]),
     ("kc_allreduce_bf16_peer", ci, [ctypes.POINTER(vp), ctypes.POINTER(vp), ci, ci, cl, vp]),
+    ("kc_allreduce_bf16_nvls", ci, [vp, ci, ci, cl, ci, vp]),
     ("kc_peer_barrier", ci, [ctypes.POINTER(vp), ci, ci, ci, ctypes.c_uint64, vp, vp]),
     ("kc_ipc_handle_bytes", ci, []),
     ("kc_ipc_alloc", ci, [ctypes.POINTER(vp), ctypes.c_size_t]),

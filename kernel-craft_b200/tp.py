@@ -222,6 +222,38 @@ class PeerBuffers:
             self._own = ctypes.c_void_p()
 
 
+class SymmetricBuffer:
+    """A device buffer allocated on every rank and bound to one NVLink
+    multicast object (torch's symmetric memory does the allocation, the
+    handle exchange and the binding): ``local`` is this rank's copy,
+    ``multicast_ptr`` the address through which multimem instructions reach
+    every rank's copy at once.  Raises RuntimeError where the platform offers
+    no multicast (no NVSwitch, or a driver without it)."""
+
+    def __init__(self, shape, dtype, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.group = group
+        grp = group if group is not None else dist.group.WORLD
+        n = 1
+        for d in shape:
+            n *= d
+        flat = symm_mem.empty(n, dtype=dtype, device=torch.device("cuda", torch.cuda.current_device()))
+        self.handle = symm_mem.rendezvous(flat, grp)
+        self.local = flat.view(tuple(shape))
+        self.multicast_ptr = int(getattr(self.handle, "multicast_ptr", 0) or 0)
+        if not self.multicast_ptr:
+            raise RuntimeError("no NVLink multicast on this platform (symmetric memory has no "
+                               "multicast address)")
+        if self.multicast_ptr % 16:
+            raise RuntimeError("multicast address not 16-byte aligned")
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.handle = None
+        self.local = None
+
+
 def _from_blob(ptr: int, shape, dtype, device: int) -> torch.Tensor:
     """A tensor viewing device memory owned elsewhere (lifetime managed by the
     caller), through the __cuda_array_interface__ protocol."""
@@ -295,8 +327,8 @@ class RowParallelFP8:
 
     def __init__(self, M: int, N: int, group=None, reduce: str = "peer", chunks: int = 4,
                  comm_sms: int = 16):
-        if reduce not in ("peer", "nccl", "overlap"):
-            raise ValueError("reduce must be 'peer', 'nccl' or 'overlap'")
+        if reduce not in ("peer", "nccl", "overlap", "nvls"):
+            raise ValueError("reduce must be 'peer', 'nccl', 'overlap' or 'nvls'")
         self.chunks, self.comm_sms = chunks, comm_sms
         self.reduce = reduce
         self.group = group
@@ -305,13 +337,21 @@ class RowParallelFP8:
         self.M, self.N = M, N
         if (M * N) % (8 * self.world):
             raise ValueError("M * N must be a multiple of 8 * world")
+        self.barrier = PeerBarrier(group)
+        if reduce == "nvls":
+            # one symmetric bf16 buffer: the GEMM writes this rank's partial
+            # into its own copy, the switch sums the copies in place
+            self.symm = SymmetricBuffer((M, N), torch.bfloat16, group)
+            self.out = self.symm.local
+            self.comm = torch.cuda.Stream()
+            self._events = []
+            return
         self.part_bufs = PeerBuffers(M * N * 2, group)
         self.out_bufs = PeerBuffers(M * N * 2, group)
         self.partial = self.part_bufs.local((M, N), torch.bfloat16)
         self.out = self.out_bufs.local((M, N), torch.bfloat16)
         self._parts = (ctypes.c_void_p * self.world)(*self.part_bufs.ptrs)
         self._outs = (ctypes.c_void_p * self.world)(*self.out_bufs.ptrs)
-        self.barrier = PeerBarrier(group)
 
     def __call__(self, a_codes_shard, sa, w_codes_shard, sw, entry_barrier: bool = True) -> torch.Tensor:
         """entry_barrier: wait until no rank still reads the previous call's
@@ -325,6 +365,8 @@ class RowParallelFP8:
         if self.reduce == "overlap":   # row blocks: block i's all-reduce under block i+1's GEMM
             return row_parallel_fp8_overlap(a_codes_shard, sa, w_codes_shard, sw, self.out,
                                             self.chunks, self.comm_sms, self.group)
+        if self.reduce == "nvls":
+            return self._nvls(a_codes_shard, sa, w_codes_shard, sw, Kr, entry_barrier)
         if entry_barrier:
             self.barrier()
         check(l.kc_gemm_fp8(ctypes.c_void_p(a_codes_shard.data_ptr()), ctypes.c_void_p(sa.data_ptr()),
@@ -337,9 +379,50 @@ class RowParallelFP8:
         self.barrier()      # every slice is in every output
         return self.out
 
+    def _nvls(self, a, sa, w, sw, Kr, entry_barrier):
+        """Row blocks of the output: block i's GEMM on the current stream (on
+        all but comm_sms SMs when there is more than one block), then on the
+        comm stream a peer barrier (block i complete on every rank) and the
+        in-switch sum of block i, under block i+1's GEMM; a last barrier on
+        the comm stream (every slice in every copy), which the current
+        stream waits for."""
+        l = lib()
+        M, N = self.M, self.N
+        chunks = max(1, min(self.chunks, (M + 127) // 128))
+        rows = -(-M // chunks)
+        rows = -(-rows // 128) * 128                 # whole 128-row tiles per block
+        sms = torch.cuda.get_device_properties(self.out.device).multi_processor_count
+        gemm_ctas = sms if chunks == 1 else max(1, sms - self.comm_sms)
+        comm_ctas = 0 if chunks == 1 else 8 * self.comm_sms
+        main = torch.cuda.current_stream()
+        if entry_barrier:
+            self.barrier()
+        self.comm.wait_stream(main)
+        mc = self.symm.multicast_ptr
+        for m0 in range(0, M, rows):
+            mc_rows = min(rows, M - m0)
+            check(l.kc_gemm_fp8_ctas(ctypes.c_void_p(a[m0:].data_ptr()), ctypes.c_void_p(sa[m0:].data_ptr()),
+                                     ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(sw.data_ptr()),
+                                     ctypes.c_void_p(self.out[m0:].data_ptr()), 0, mc_rows, N, Kr, N,
+                                     gemm_ctas, _stream()))
+            ev = torch.cuda.Event()
+            ev.record(main)
+            with torch.cuda.stream(self.comm):
+                self.comm.wait_event(ev)
+                self.barrier()                       # block complete on every rank
+                check(l.kc_allreduce_bf16_nvls(ctypes.c_void_p(mc + 2 * m0 * N), self.world, self.rank,
+                                               mc_rows * N, comm_ctas, _stream()))
+        with torch.cuda.stream(self.comm):
+            self.barrier()                           # every slice is in every copy
+        main.wait_stream(self.comm)
+        return self.out
+
     def close(self) -> None:
         torch.cuda.synchronize()
         self.barrier.close()
+        if self.reduce == "nvls":
+            self.symm.close()
+            return
         self.part_bufs.close()
         self.out_bufs.close()
 

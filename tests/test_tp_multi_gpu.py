@@ -8,7 +8,9 @@ GEMM + bf16 sum -- by NCCL all-reduce (also row block by row block, each
 block's all-reduce overlapping the next block's GEMM) and by the peer-memory kernel
 kc_allreduce_bf16_peer -- against the single-GPU FP8 GEMM, normwise <= 1e-2
 (bf16 partials are rounded before the sum); the peer sum is identical on
-every rank.  MLP block (tp.MLPBlockW4A16, the reference's col-parallel ->
+every rank; so is the in-switch sum (RowParallelFP8 reduce="nvls":
+multimem.ld_reduce / multimem.st through NVLink SHARP, where the platform has
+multicast).  MLP block (tp.MLPBlockW4A16, the reference's col-parallel ->
 GELU -> row-parallel chain): the sharded block against the two unsharded
 GEMMs on one GPU, normwise <= 1e-5 (the activations are the same bits; only
 the fp32 order of the K sum differs).  Skipped with fewer than 2 GPUs.
@@ -89,6 +91,22 @@ def _rank_main(rank, world, port, out_dir):
         dist.all_gather(gathered, y2.clone())
         row_same = all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16)) for g in gathered)
         rp.close()
+        # the in-switch sum (NVLink SHARP multicast), two row blocks, twice in a
+        # row (the second call reuses the symmetric buffer behind the barriers)
+        try:
+            rn = tp.RowParallelFP8(M2, N2, reduce="nvls", chunks=2)
+        except RuntimeError:
+            nvls_err, nvls_same = -1.0, -1.0           # no multicast on this platform
+        else:
+            rn(qa_s, sa, qw_s, sw)
+            y4 = rn(qa_s, sa, qw_s, sw, entry_barrier=True).clone()
+            torch.cuda.synchronize()
+            nvls_err = float((y4.float() - ref).abs().max() / ref.abs().max())
+            gathered = [torch.empty_like(y4) for _ in range(world)]
+            dist.all_gather(gathered, y4)
+            nvls_same = float(all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16))
+                                  for g in gathered))
+            rn.close()
 
         # MLP block: W1 [I, H] by rows, W2 [H, I] by the same columns, one all-reduce
         M3, H3, I3 = 200, 512, 2048
@@ -111,7 +129,8 @@ def _rank_main(rank, world, port, out_dir):
         mlp_err = float((y3 - y_full).abs().max() / y_full.abs().max())
         status = l.kc_get_device_status()
         np.save(os.path.join(out_dir, f"rank{rank}.npy"),
-                np.array([col_ok, row_err, status, row_same, mlp_err], dtype=np.float64))
+                np.array([col_ok, row_err, status, row_same, mlp_err, nvls_err, nvls_same],
+                         dtype=np.float64))
         col.close()
     finally:
         dist.destroy_process_group()
@@ -123,9 +142,12 @@ def test_tensor_parallel_two_gpus(tmp_path):
     import torch.multiprocessing as mp
     mp.spawn(_rank_main, args=(WORLD, _free_port(), str(tmp_path)), nprocs=WORLD, join=True)
     for r in range(WORLD):
-        col_ok, row_err, status, row_same, mlp_err = np.load(tmp_path / f"rank{r}.npy")
+        col_ok, row_err, status, row_same, mlp_err, nvls_err, nvls_same = np.load(tmp_path / f"rank{r}.npy")
         assert row_same == 1.0, "peer all-reduce outputs differ between ranks"
         assert col_ok == 1.0, f"rank {r}: gathered W4A16 output differs from the single-GPU GEMM"
         assert row_err <= 1e-2, f"rank {r}: row-parallel FP8 error {row_err}"
         assert mlp_err <= 1e-5, f"rank {r}: MLP block error {mlp_err}"
+        if nvls_err >= 0:
+            assert nvls_err <= 1e-2, f"rank {r}: row-parallel FP8 (in-switch sum) error {nvls_err}"
+            assert nvls_same == 1.0, "in-switch sum outputs differ between ranks"
         assert status == 0

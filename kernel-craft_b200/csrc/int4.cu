@@ -188,6 +188,13 @@ __device__ __forceinline__ float chunk_dot(const uint4& v, uint32_t x0, uint64_t
 // reads over all 32 banks.
 __host__ __device__ constexpr size_t xs_bytes(int cols) { return (size_t)cols / 32 * 144; }
 
+// GSH >= 0: the group size is 32 << GSH and cols a multiple of 4096, so
+// every lane owns four chunks per 128-chunk block and each load's address is
+// the lane's base plus a constant (group index (lane >> GSH) + (32 >> GSH) u,
+// zero-point byte (lane >> (GSH + 1)) + (16 >> GSH) u, its nibble fixed per
+// lane); GSH = -1 handles any cols multiple of 32 and group size multiple of
+// 32 with computed indices.
+template <int GSH>
 __global__ void __launch_bounds__(1024, 1) gemv_int4_f32_vec(const uint8_t* __restrict__ packed,
                                                              const float* __restrict__ scales,
                                                              const uint8_t* __restrict__ zeros,
@@ -229,14 +236,28 @@ __global__ void __launch_bounds__(1024, 1) gemv_int4_f32_vec(const uint8_t* __re
     uint32_t zb[kU];
     int g[kU];
     auto issue = [&](int jb) {
+        if constexpr (GSH >= 0) {
+            // this lane's bases in row r's 128-chunk block (jb - lane) / 128
+            const int blk = (jb - lane) >> 7;
+            const uint8_t* pl = packed + (long)r * (cols / 2) + 2048 * blk + 16 * lane;
+            const float* sl = scales + (long)r * sc + (128 >> GSH) * blk + (lane >> GSH);
+            const uint8_t* zl = zeros + (long)r * zc + (64 >> GSH) * blk + (lane >> (GSH + 1));
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            const int j = jb + 32 * u;
-            if (j < cpr) {
-                g[u] = gs_shift >= 0 ? (32 * j) >> gs_shift : (32 * j) / gs;
-                v[u] = kc_ldg_stream(p + 16 * j);
-                s[u] = __ldg(srow + g[u]);
-                zb[u] = __ldg(zrow + (g[u] >> 1));
+            for (int u = 0; u < kU; ++u) {
+                v[u] = kc_ldg_stream(pl + 512 * u);
+                s[u] = __ldg(sl + (32 >> GSH) * u);
+                zb[u] = __ldg(zl + (16 >> GSH) * u);
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int j = jb + 32 * u;
+                if (j < cpr) {
+                    g[u] = gs_shift >= 0 ? (32 * j) >> gs_shift : (32 * j) / gs;
+                    v[u] = kc_ldg_stream(p + 16 * j);
+                    s[u] = __ldg(srow + g[u]);
+                    zb[u] = __ldg(zrow + (g[u] >> 1));
+                }
             }
         }
     };
@@ -263,13 +284,15 @@ __global__ void __launch_bounds__(1024, 1) gemv_int4_f32_vec(const uint8_t* __re
     const uint64_t nexp2 = f2pack(-8388608.f, -8388608.f);
     while (true) {
         float acc = 0.f;
+#pragma unroll 1
         for (int jb = lane; jb < cpr; jb += 32 * kU) {
             if (jb != lane) issue(jb);
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
                 const int j = jb + 32 * u;
-                if (j >= cpr) break;
-                const uint32_t z = (g[u] & 1) ? (zb[u] >> 4) : (zb[u] & 15u);
+                if (GSH < 0 && j >= cpr) break;
+                const uint32_t z = GSH >= 0 ? (zb[u] >> (((threadIdx.x >> (GSH < 0 ? 0 : GSH)) & 1u) << 2)) & 15u
+                                            : ((g[u] & 1) ? (zb[u] >> 4) : (zb[u] & 15u));
                 const uint32_t xj = xs0 + 144u * (uint32_t)j;
                 float xsum;
                 asm volatile("ld.shared.f32 %0, [%1];" : "=f"(xsum) : "r"(xj + 128u));
@@ -442,8 +465,13 @@ int kc_gemv_int4_f32(const uint8_t* packed, const float* scales, const uint8_t* 
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        KC_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_int4_f32_vec, packed, scales, zeros, x, y, rows, cols,
-                                       gs, gs_shift, 0x4B000000u),
+        // group sizes 32..256 with cols a multiple of 4096: constant offsets
+        const int gsh = (cols % 4096 == 0 && gs_shift >= 5 && gs_shift <= 8) ? gs_shift - 5 : -1;
+        auto kern = gsh == 0 ? gemv_int4_f32_vec<0> : gsh == 1 ? gemv_int4_f32_vec<1>
+                  : gsh == 2 ? gemv_int4_f32_vec<2> : gsh == 3 ? gemv_int4_f32_vec<3>
+                  : gemv_int4_f32_vec<-1>;
+        KC_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, packed, scales, zeros, x, y, rows, cols, gs, gs_shift,
+                                       0x4B000000u),
                     "gemv_int4_f32 launch");
         return KC_OK;
     }

@@ -81,7 +81,12 @@ def test_reference_kats(cuda, golden):
 
 @pytest.mark.parametrize("rows,cols,gs", [(4096, 4096, 128), (37, 384, 128), (16, 96, 32),
                                           (8, 256, 64), (5, 24, 8), (3, 6, 2), (1, 2, 2),
-                                          (64, 1536, 512)])
+                                          (64, 1536, 512),
+                                          # the constant-offset GEMV: every group size 32..256,
+                                          # two 4096-column blocks per row, more rows than
+                                          # one pass of the grid's warps
+                                          (300, 4096, 32), (200, 8192, 64), (150, 8192, 128),
+                                          (5000, 4096, 256)])
 @pytest.mark.parametrize("zeros_mode", ["zero", "eight", "random"])
 def test_dequant_and_gemv_reference_abi(cuda, rows, cols, gs, zeros_mode):
     packed, scales, zeros, x = _ref_int4_case(rows, cols, gs, zeros_mode, seed=rows + cols)

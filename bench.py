@@ -457,7 +457,14 @@ class GemmW4A16(Workload):
         self.col = None
         if world > 1:
             import tp
-            self.col = tp.ColParallelW4A16(M, N, K, GROUP)
+            # each output tile leaves the GPU once through the switch's multicast
+            # from 4 ranks on (once per peer with the TMA stores); at 2 ranks the
+            # multicast would also route the local copy over NVLink
+            store = os.environ.get("KC_TP_STORE", "peer" if world == 2 else "nvls")
+            try:
+                self.col = tp.ColParallelW4A16(M, N, K, GROUP, store=store)
+            except RuntimeError:        # no NVLink multicast
+                self.col = tp.ColParallelW4A16(M, N, K, GROUP, store="peer")
             self.scaling = "strong"
         self.i = 0
 
@@ -494,9 +501,12 @@ class GemmW4A16(Workload):
     def parallelism(self):
         if self.world == 1:
             return "single GPU"
-        return (f"column parallel x{self.world}: N/{self.world} weight rows per GPU, "
-                "output tiles stored into every GPU's [M, N] buffer by the GEMM epilogue "
-                "over NVLink (fused all-gather), one peer-flag barrier per step")
+        how = ("TMA-stored into every GPU's [M, N] buffer by the GEMM epilogue over NVLink"
+               if self.col.store == "peer" else
+               "written once by the GEMM epilogue through the NVSwitch multicast (multimem.st), "
+               "which stores them into every GPU's [M, N] buffer")
+        return (f"column parallel x{self.world}: N/{self.world} weight rows per GPU, output tiles "
+                f"{how} (fused all-gather), one peer-flag barrier per step")
 
     def config(self):
         return {"workload": self.workload_id, "M": self.M, "N": self.N, "K": self.K,
@@ -558,14 +568,14 @@ class GemmW4A16(Workload):
         ref = torch.empty(M, N, dtype=torch.bfloat16, device=self.dev)
         self.kc_lib.check(self.l.kc_gemm_w4a16(x.data_ptr(), p.data_ptr(), s.data_ptr(),
                                                ref.data_ptr(), 0, M, N, K, GROUP, N, self.s_ptr))
-        col = tp.ColParallelW4A16(M, N, K, GROUP)
+        col = tp.ColParallelW4A16(M, N, K, GROUP, store=self.col.store)
         ps, ss = tp.shard_w4_rows(p, s, self.world, self.rank)
         out = col(x, ps, ss).clone()
         torch.cuda.synchronize()
         col.close()
         ok = bool(torch.equal(out, ref))
-        return ok, {"check": f"column parallel x{self.world} on [{M}, {K}] x [{N}, {K}]^T "
-                             "vs the single-GPU kc_gemm_w4a16, bit-equal",
+        return ok, {"check": f"column parallel x{self.world} ({self.col.store} stores) on "
+                             f"[{M}, {K}] x [{N}, {K}]^T vs the single-GPU kc_gemm_w4a16, bit-equal",
                     "passed": ok, "normwise_err": _normwise(out, ref)}
 
     def close(self):
@@ -1456,11 +1466,12 @@ def main(argv=None) -> int:
     stream = torch.cuda.current_stream()
     s_ptr = ctypes.c_void_p(stream.cuda_stream)
 
+    # a failed correctness gate (agreed by every rank) prints its error line and
+    # the run goes on to the next workload, so the headline still prints; the
+    # exit status stays non-zero
     rc = 0
     for name in _selected(args):
-        rc = run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, local)
-        if rc:
-            break
+        rc = run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, local) or rc
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -356,6 +356,38 @@ KC_API int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed
                                    const uint16_t* scales_shard, void* const* outs, int nranks,
                                    int rank, int M, int N_shard, int K, int group_size,
                                    cudaStream_t stream);
+/* As kc_gemm_w4a16_allgather, with every output tile written once through
+ * NVLink SHARP: mc_out is the multicast address of a bf16 [M, N_shard*nranks]
+ * buffer bound on every rank (e.g. a symmetric allocation's multicast
+ * pointer); the epilogue stores each tile with multimem.st and the switch
+ * writes it into every rank's copy, so a tile leaves the GPU once instead of
+ * once per peer.  Synchronization as for kc_gemm_w4a16_allgather. */
+KC_API int kc_gemm_w4a16_allgather_mc(const uint16_t* x_bf16, const uint8_t* packed_shard,
+                                      const uint16_t* scales_shard, void* mc_out, int nranks, int rank,
+                                      int M, int N_shard, int K, int group_size, cudaStream_t stream);
+
+/* Row-parallel FP8 GEMM with its all-reduce fused into the epilogue (one
+ * process per GPU; the reference composes launch_row_parallel_linear with
+ * launch_ring_allreduce_nccl, tensor_parallel.cu:235, tensor_parallel_nccl.cu:105).
+ * Each rank holds the K shard of both code matrices (a_codes_shard [M, K_shard],
+ * w_codes_shard [N, K_shard]) and the full-row scales sa [M], sw [N]; output
+ * rows are owned in nranks equal blocks.  A partial tile of another owner is
+ * written (bf16) into that owner's receive slot and announced by a flag; the
+ * owner adds the received partials to its fp32 tile and writes the bf16 sum
+ * into every rank's output, so every outs[r] ends with the full [M, N] bf16
+ * result.  outs[r] / recvs[r] / flags[r]: rank r's output [M, N] bf16, receive
+ * slots (nranks - 1) x [M / nranks, N] bf16 and flags (nranks - 1) x
+ * (M / 128 / nranks) x (N / 256) ints (zeroed once), as mapped in this process.
+ * Every rank passes the same, increasing epoch (> 0).  The ranks' launches
+ * must be aligned (a kc_peer_barrier before it) and the outputs are complete
+ * once every rank's launch has finished (a barrier after it).  A flag wait
+ * gives up after timeout_ns (0: KC_PEER_BARRIER_DEFAULT_TIMEOUT_NS), records
+ * KC_ERR_TIMEOUT and makes the affected tiles NaN.
+ * M % (128 * nranks) == 0, N % 256 == 0, K_shard % 16 == 0, 2 <= nranks <= KC_MAX_RANKS. */
+KC_API int kc_gemm_fp8_allreduce(const int8_t* a_codes_shard, const float* sa, const int8_t* w_codes_shard,
+                                 const float* sw, void* const* outs, void* const* recvs, int* const* flags,
+                                 int nranks, int rank, int epoch, int M, int N, int K_shard,
+                                 uint64_t timeout_ns, cudaStream_t stream);
 
 /* bf16 sum all-reduce over NVLink peer memory (one process per GPU; the
  * reference's counterpart is launch_ring_allreduce_nccl, fp32,
@@ -399,8 +431,8 @@ KC_API int kc_allreduce_bf16_nvls(void* mc, int nranks, int rank, long count, in
  * records KC_ERR_TIMEOUT for kc_get_device_status(), writes KC_ERR_TIMEOUT
  * into *status_host when status_host is not NULL (pinned host memory, so the
  * host can poll it without synchronizing), and every kc_allreduce_bf16_peer
- * of the process writes NaN from then on, until kc_get_device_status()
- * clears the status. */
+ * and kc_allreduce_bf16_nvls of the process writes NaN from then on, until
+ * kc_get_device_status() clears the status. */
 #define KC_PEER_BARRIER_DEFAULT_TIMEOUT_NS 2000000000ull    /* 2 s */
 #define KC_PEER_BARRIER_MAX_TIMEOUT_NS     600000000000ull  /* 10 min */
 KC_API int kc_peer_barrier(int* const* flags, int nranks, int rank, int epoch, uint64_t timeout_ns,

@@ -34,6 +34,23 @@ constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
 constexpr uint32_t kTmemCols = 512;
 
+// Row-parallel sum fused into the epilogue (RS kernels): every rank computes
+// the partial product of its K shard for all tiles; output rows are owned in R
+// equal blocks.  A rank walks the owners' blocks starting after its own, so
+// its own block comes last: a tile of another owner is written (bf16) into
+// that owner's receive slot over NVLink and announced with a flag; a tile of
+// its own waits for the R - 1 flags of that tile, adds the received partials
+// to its fp32 accumulator and writes the bf16 sum into every rank's output.
+// Per GPU that sends (R-1)/R of the output as partials and (R-1)/R as sums,
+// both under the MMAs of the following tiles.
+struct RsParams {
+    __nv_bfloat16* outs[KC_MAX_RANKS];   // every rank's [M, N] bf16 output (pitch N)
+    __nv_bfloat16* recv[KC_MAX_RANKS];   // every rank's receive slots: (R - 1) x [M / R, N] bf16
+    int* flags[KC_MAX_RANKS];            // every rank's flags: (R - 1) x tiles per owner block
+    int nranks, rank, epoch;
+    uint64_t timeout_ns;
+};
+
 struct alignas(64) Params {
     CUtensorMap amap;   // A codes {K, M}, box {128, 128}, 128-byte swizzle
     CUtensorMap wmap;   // W codes {K, N}, box {128, 256}, 128-byte swizzle
@@ -43,7 +60,27 @@ struct alignas(64) Params {
     int M, N, K, ldc;
     int out_f32;
     int tiles_m, tiles_n;
+    RsParams rs;
 };
+
+// Linear tile L -> its output tile (m0, n0); for RS also the owner and the
+// tile's index within the owner's block.
+template <bool RS>
+__device__ __forceinline__ void tile_coords(const Params& P, int L, int& m0, int& n0, int& owner, int& j) {
+    if constexpr (!RS) {
+        m0 = (L % P.tiles_m) * BM;
+        n0 = (L / P.tiles_m) * BN;
+        owner = 0;
+        j = L;
+    } else {
+        const int R = P.rs.nranks, tmo = P.tiles_m / R, per = tmo * P.tiles_n;
+        const int b = L / per;
+        j = L - b * per;
+        owner = (P.rs.rank + 1 + b) % R;
+        m0 = (owner * tmo + j % tmo) * BM;
+        n0 = (j / tmo) * BN;
+    }
+}
 
 struct Smem {
     uint8_t a[kStages][kABytes];   // 1024-byte aligned (swizzle atoms)
@@ -62,6 +99,7 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+template <bool RS>
 __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_constant__ Params P) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled operand tiles
@@ -102,7 +140,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
             uint32_t it = 0;   // loads issued; nothing more is issued after a failed wait
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
-                const int m0 = (tile % P.tiles_m) * BM, n0 = (tile / P.tiles_m) * BN;
+                int m0, n0, owner, j;
+                tile_coords<RS>(P, tile, m0, n0, owner, j);
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     const uint32_t s = it % kStages, ph = (it / kStages) & 1u;
                     if (!(ok = sm100::mbar_wait_or_abort(&S.empty[s], ph ^ 1u, abort))) break;
@@ -151,18 +190,48 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
     } else {
         // -------------------------------- epilogue --------------------------------
         const int q = warp & 3;                      // TMEM lane quarter of this warp
+        const int et = threadIdx.x - 64;             // 0..127 over the epilogue warps
         uint32_t t = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
             const uint32_t acc = t & 1u;
-            const int m0 = (tile % P.tiles_m) * BM, n0 = (tile / P.tiles_m) * BN;
+            int m0, n0, owner, j;
+            tile_coords<RS>(P, tile, m0, n0, owner, j);
             const int m = m0 + q * 32 + lane;
             const float sam = (m < P.M) ? __ldg(P.sa + m) : 0.f;
             const bool waited = sm100::mbar_wait_or_abort(&S.tmem_full[acc], (t >> 1) & 1u, abort);
             sm100::tc_fence_after();
+            const bool mine = !RS || owner == P.rs.rank;
+            bool peers_ok = true;
+            if constexpr (RS) {
+                // a tile of this rank's block: wait for every peer's partial of it
+                // (bounded; a peer that never delivers makes the tile NaN)
+                if (mine) {
+                    if (et == 0) {
+                        const int per = (P.tiles_m / P.rs.nranks) * P.tiles_n;
+                        const uint64_t t0 = sm100::globaltimer();
+                        for (int sl = 0; sl < P.rs.nranks - 1 && peers_ok; ++sl) {
+                            const int* f = P.rs.flags[P.rs.rank] + sl * per + j;
+                            while (true) {
+                                int v;
+                                asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                                if ((int)((unsigned)v - (unsigned)P.rs.epoch) >= 0) break;
+                                if (*abort || sm100::globaltimer() - t0 > P.rs.timeout_ns) {
+                                    sm100::record_status(KC_ERR_TIMEOUT);
+                                    *abort = 1;
+                                    peers_ok = false;
+                                    break;
+                                }
+                            }
+                        }
+                    }
+                    sm100::named_sync(1, 128);
+                    peers_ok = !*abort;
+                }
+            }
             // after a wait gave up anywhere in the CTA the accumulator is not a
             // result: the tile is written as NaN, so a timeout cannot pass for
             // plausible output (kc_get_device_status reports it as well)
-            const bool poison = !waited || *abort;
+            const bool poison = !waited || *abort || !peers_ok;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
@@ -180,6 +249,57 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
                     v[4 * i + 1] = __uint_as_float(r[4 * i + 1]) * sam * s4.y;
                     v[4 * i + 2] = __uint_as_float(r[4 * i + 2]) * sam * s4.z;
                     v[4 * i + 3] = __uint_as_float(r[4 * i + 3]) * sam * s4.w;
+                }
+                if constexpr (RS) {
+                    const int R = P.rs.nranks, rows = P.M / R;
+                    if (!mine) {
+                        // this rank's partial into the owner's receive slot
+                        const int sl = (P.rs.rank - owner - 1 + R) % R;
+                        __nv_bfloat16* o = P.rs.recv[owner] + ((size_t)sl * rows + (m - owner * rows)) * P.N + nb;
+                        if (poison)
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7FC00000);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            reinterpret_cast<uint4*>(o)[i] =
+                                make_uint4(bf16x2_bits(v[8 * i], v[8 * i + 1]),
+                                           bf16x2_bits(v[8 * i + 2], v[8 * i + 3]),
+                                           bf16x2_bits(v[8 * i + 4], v[8 * i + 5]),
+                                           bf16x2_bits(v[8 * i + 6], v[8 * i + 7]));
+                        continue;
+                    }
+                    // the owner: add the peers' partials (slots in order), then
+                    // the sum into every rank's output
+                    for (int sl = 0; sl < R - 1; ++sl) {
+                        const uint4* in = reinterpret_cast<const uint4*>(
+                            P.rs.recv[P.rs.rank] + ((size_t)sl * rows + (m - P.rs.rank * rows)) * P.N + nb);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const uint4 w = __ldcg(in + i);
+                            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                v[8 * i + 2 * e] += __uint_as_float(ww[e] << 16);
+                                v[8 * i + 2 * e + 1] += __uint_as_float(ww[e] & 0xFFFF0000u);
+                            }
+                        }
+                    }
+                    if (poison)
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7FC00000);
+                    uint4 o4[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        o4[i] = make_uint4(bf16x2_bits(v[8 * i], v[8 * i + 1]), bf16x2_bits(v[8 * i + 2], v[8 * i + 3]),
+                                           bf16x2_bits(v[8 * i + 4], v[8 * i + 5]),
+                                           bf16x2_bits(v[8 * i + 6], v[8 * i + 7]));
+                    for (int d = 0; d < R; ++d) {
+                        const int r = (P.rs.rank + d) % R;   // own copy first
+                        uint4* o = reinterpret_cast<uint4*>(P.rs.outs[r] + (size_t)m * P.N + nb);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) o[i] = o4[i];
+                    }
+                    continue;
                 }
                 if (poison)
 #pragma unroll
@@ -212,7 +332,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
             sm100::tc_fence_before();
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(&S.tmem_empty[acc]);
+            if constexpr (RS) {
+                // a partial for another owner: every thread's stores, then the flag
+                if (!mine) {
+                    __threadfence_system();
+                    sm100::named_sync(1, 128);
+                    if (et == 0) {
+                        const int R = P.rs.nranks, per = (P.tiles_m / R) * P.tiles_n;
+                        const int sl = (P.rs.rank - owner - 1 + R) % R;
+                        int* f = P.rs.flags[owner] + sl * per + j;
+                        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(f), "r"(P.rs.epoch) : "memory");
+                    }
+                }
+            }
         }
+        if constexpr (RS) __threadfence_system();   // the sums, before the barrier after the kernel
     }
 
     // teardown: every MMA has been consumed by the epilogue before this barrier
@@ -258,14 +392,68 @@ int kc_gemm_fp8_ctas(const int8_t* a_codes, const float* sa, const int8_t* w_cod
     P.tiles_m = (M + BM - 1) / BM;
     P.tiles_n = (N + BN - 1) / BN;
     const size_t smem = sizeof(Smem) + 1024;
-    KC_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    KC_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem),
                 "gemm_fp8 shared-memory attribute");
     const int tiles = P.tiles_m * P.tiles_n;
     const int ctas = max_ctas > 0 ? std::min(max_ctas, kc::sm_count()) : kc::sm_count();
     const int grid = std::min(tiles, ctas);
-    gemm_fp8_kernel<<<grid, kThreads, smem, stream>>>(P);
+    gemm_fp8_kernel<false><<<grid, kThreads, smem, stream>>>(P);
     return kc::check_launch("gemm_fp8");
+}
+
+int kc_gemm_fp8_allreduce(const int8_t* a_codes_shard, const float* sa, const int8_t* w_codes_shard,
+                          const float* sw, void* const* outs, void* const* recvs, int* const* flags,
+                          int nranks, int rank, int epoch, int M, int N, int K_shard, uint64_t timeout_ns,
+                          cudaStream_t stream) {
+    KC_REQUIRE(a_codes_shard && sa && w_codes_shard && sw && outs && recvs && flags, KC_ERR_INVALID_ARG,
+               "null pointer argument");
+    KC_REQUIRE(nranks >= 2 && nranks <= KC_MAX_RANKS && rank >= 0 && rank < nranks, KC_ERR_INVALID_ARG,
+               "rank %d of %d: 2..%d ranks", rank, nranks, KC_MAX_RANKS);
+    KC_REQUIRE(M > 0 && M % (BM * nranks) == 0, KC_ERR_INVALID_ARG,
+               "M=%d must be a positive multiple of %d x nranks", M, BM);
+    KC_REQUIRE(N > 0 && N % BN == 0, KC_ERR_INVALID_ARG, "N=%d must be a positive multiple of %d", N, BN);
+    KC_REQUIRE(K_shard > 0 && K_shard % 16 == 0, KC_ERR_INVALID_ARG,
+               "K_shard=%d must be a positive multiple of 16", K_shard);
+    KC_REQUIRE(timeout_ns <= KC_PEER_BARRIER_MAX_TIMEOUT_NS, KC_ERR_INVALID_ARG, "timeout above the maximum");
+    KC_REQUIRE(kc::aligned(a_codes_shard, 16) && kc::aligned(w_codes_shard, 16) && kc::aligned(sw, 16),
+               KC_ERR_ALIGNMENT, "operands must be 16-byte aligned");
+    Params P{};
+    for (int r = 0; r < nranks; ++r) {
+        KC_REQUIRE(outs[r] && recvs[r] && flags[r] && kc::aligned(outs[r], 16) && kc::aligned(recvs[r], 16) &&
+                       kc::aligned(flags[r], 4),
+                   KC_ERR_ALIGNMENT, "buffers of rank %d null or misaligned", r);
+        P.rs.outs[r] = static_cast<__nv_bfloat16*>(outs[r]);
+        P.rs.recv[r] = static_cast<__nv_bfloat16*>(recvs[r]);
+        P.rs.flags[r] = flags[r];
+    }
+    P.rs.nranks = nranks;
+    P.rs.rank = rank;
+    P.rs.epoch = epoch;
+    P.rs.timeout_ns = timeout_ns ? timeout_ns : KC_PEER_BARRIER_DEFAULT_TIMEOUT_NS;
+    int st = kc::encode_2d(&P.amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_codes_shard, (uint64_t)K_shard, (uint64_t)M,
+                           (uint64_t)K_shard, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = kc::encode_2d(&P.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes_shard, (uint64_t)K_shard, (uint64_t)N,
+                       (uint64_t)K_shard, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    P.sa = sa;
+    P.sw = sw;
+    P.out = outs[rank];
+    P.M = M;
+    P.N = N;
+    P.K = K_shard;
+    P.ldc = N;
+    P.out_f32 = 0;
+    P.tiles_m = M / BM;
+    P.tiles_n = N / BN;
+    const size_t smem = sizeof(Smem) + 1024;
+    KC_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem),
+                "gemm_fp8 shared-memory attribute");
+    const int tiles = P.tiles_m * P.tiles_n;
+    gemm_fp8_kernel<true><<<std::min(tiles, kc::sm_count()), kThreads, smem, stream>>>(P);
+    return kc::check_launch("gemm_fp8_allreduce");
 }
 
 int kc_gemm_fp8(const int8_t* a_codes, const float* sa, const int8_t* w_codes, const float* sw,

@@ -62,6 +62,7 @@ struct alignas(64) Params {
     const __half* scales;
     const uint8_t* zeros;   // per-group zero points u8[N, K/gs]; null: 8 (symmetric GPTQ)
     void* out;
+    uint8_t* mc_out;        // multicast address of every rank's bf16 output (pitch ldc), or null
     int M, N, K, gs, ldc, out_f32, tma_out;
     int act;       // KC_ACT_NONE or KC_ACT_GELU_QUICK, applied in the epilogue
     int ndst;      // destination buffers of each tile (1, or the ranks of an all-gather)
@@ -329,9 +330,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
             // plausible output (kc_get_device_status reports it as well)
             const float nan = __int_as_float(0x7FC00000);
             const bool poison = !waited || *abort;
-            if (P.tma_out) {
+            if (P.tma_out || P.mc_out) {
                 // the previous tile's TMA stores have finished reading the staging tile
-                if (store_lead) sm100::bulk_wait_group_read0();
+                // (multicast stores take their data from registers: nothing to wait for)
+                if (store_lead && P.tma_out) sm100::bulk_wait_group_read0();
                 sm100::named_sync(1, 128);
 #pragma unroll 1
                 for (int c = 0; c < BT / 64; ++c) {
@@ -355,14 +357,35 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
                             __float2bfloat16_rn(poison ? nan : activate(__uint_as_float(r2[i]), P.act));
                     }
                 }
-                sm100::fence_proxy_async_smem();
-                sm100::named_sync(1, 128);   // all four strips are in the staging tile
-                if (store_lead) {
-                    // one 128-column box per destination: 256-byte rows, local
-                    // buffer or every rank's over NVLink
-                    for (int d = 0; d < P.ndst; ++d)
-                        sm100::tma_store_2d(&P.omap[d], stage, P.col_off + n0, m0);
-                    sm100::bulk_commit_group();
+                if (P.mc_out) {
+                    // every rank's copy at once through the NVSwitch: each 16-byte
+                    // piece of the tile leaves the SM once (multimem.st), the switch
+                    // writes it into all copies.  Token row r of the tile is 256
+                    // bytes (16 pieces); the 128 threads take pieces t, t + 128, ...
+                    sm100::named_sync(1, 128);   // all four strips are in the staging tile
+                    const int rows = min(BT, P.M - m0);
+                    const uint32_t stage_u32 = sm100::smem_u32(stage);
+                    const int t = threadIdx.x - kEpiWarp0 * 32;
+                    uint8_t* dst = P.mc_out + ((size_t)m0 * P.ldc + P.col_off + n0) * 2;
+#pragma unroll 4
+                    for (int i = t; i < rows * 16; i += 128) {
+                        const int r = i >> 4, v = i & 15;
+                        const uint4 d = lds128(stage_u32 + r * (BW * 2) + v * 16);
+                        asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};"
+                                     ::"l"(dst + (size_t)r * P.ldc * 2 + v * 16), "r"(d.x), "r"(d.y),
+                                       "r"(d.z), "r"(d.w)
+                                     : "memory");
+                    }
+                } else {
+                    sm100::fence_proxy_async_smem();
+                    sm100::named_sync(1, 128);   // all four strips are in the staging tile
+                    if (store_lead) {
+                        // one 128-column box per destination: 256-byte rows, local
+                        // buffer or every rank's over NVLink
+                        for (int d = 0; d < P.ndst; ++d)
+                            sm100::tma_store_2d(&P.omap[d], stage, P.col_off + n0, m0);
+                        sm100::bulk_commit_group();
+                    }
                 }
             } else {
 #pragma unroll 1
@@ -392,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_w4a16_kernel(const __grid_co
             }
         }
         if (store_lead) sm100::bulk_wait_group0();  // stores complete before the CTA exits
+        if (P.mc_out) __threadfence_system();        // the multicast stores, before the barrier after
     }
 
     sm100::tc_fence_before();
@@ -412,7 +436,7 @@ namespace {
 int launch_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint16_t* scales_f16,
                       const uint8_t* zeros, void* const* outs, int ndst, int col_off, int out_cols,
                       int out_f32, int M, int N, int K, int group_size, int ldc, int act,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, void* mc_out = nullptr) {
     KC_REQUIRE(x_bf16 && packed && scales_f16 && outs && outs[0], KC_ERR_INVALID_ARG,
                "null pointer argument");
     KC_REQUIRE(act == KC_ACT_NONE || act == KC_ACT_GELU_QUICK, KC_ERR_INVALID_ARG,
@@ -437,7 +461,8 @@ int launch_gemm_w4a16(const uint16_t* x_bf16, const uint8_t* packed, const uint1
     if (st) return st;
     bool aligned = true;
     for (int d = 0; d < ndst; ++d) aligned = aligned && outs[d] && kc::aligned(outs[d], 16);
-    P.tma_out = (!out_f32 && aligned && ldc % 8 == 0) ? 1 : 0;
+    P.tma_out = (!out_f32 && aligned && ldc % 8 == 0 && mc_out == nullptr) ? 1 : 0;
+    P.mc_out = static_cast<uint8_t*>(mc_out);
     KC_REQUIRE(ndst == 1 || P.tma_out, KC_ERR_ALIGNMENT,
                "all-gather outputs must be bf16, 16-byte aligned, with a pitch divisible by 8");
     if (P.tma_out) {
@@ -500,6 +525,24 @@ int kc_gemm_w4a16_act(const uint16_t* x_bf16, const uint8_t* packed, const uint1
     void* outs[1] = {out};
     return launch_gemm_w4a16(x_bf16, packed, scales_f16, nullptr, outs, 1, 0, N, out_f32, M, N, K,
                              group_size, ldc, act, stream);
+}
+
+int kc_gemm_w4a16_allgather_mc(const uint16_t* x_bf16, const uint8_t* packed_shard,
+                               const uint16_t* scales_shard, void* mc_out, int nranks, int rank, int M,
+                               int N_shard, int K, int group_size, cudaStream_t stream) {
+    KC_REQUIRE(mc_out != nullptr && kc::aligned(mc_out, 16), KC_ERR_ALIGNMENT,
+               "multicast output null or not 16-byte aligned");
+    KC_REQUIRE(nranks >= 1 && nranks <= KC_MAX_RANKS && rank >= 0 && rank < nranks, KC_ERR_INVALID_ARG,
+               "rank %d of %d outside 0..%d", rank, nranks, KC_MAX_RANKS - 1);
+    KC_REQUIRE(N_shard >= 0 && N_shard % BW == 0, KC_ERR_INVALID_ARG,
+               "N_shard=%d must be a multiple of %d", N_shard, BW);
+    const long cols = (long)N_shard * nranks;
+    KC_REQUIRE(cols < (1L << 31), KC_ERR_INVALID_ARG, "output too wide");
+    // outs[0] only passes the launcher's checks; every store goes through mc_out
+    void* outs[1] = {mc_out};
+    return launch_gemm_w4a16(x_bf16, packed_shard, scales_shard, nullptr, outs, 1, rank * N_shard,
+                             (int)cols, 0, M, N_shard, K, group_size, (int)cols, KC_ACT_NONE, stream,
+                             mc_out);
 }
 
 int kc_gemm_w4a16_allgather(const uint16_t* x_bf16, const uint8_t* packed_shard,

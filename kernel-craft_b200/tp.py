@@ -277,22 +277,40 @@ class ColParallelW4A16:
     full bf16 output [M, N] in this rank's shared buffer, identical on every
     rank once the call returns (the stream-ordered barrier is part of it)."""
 
-    def __init__(self, M: int, N: int, K: int, group_size: int = 128, group=None):
+    def __init__(self, M: int, N: int, K: int, group_size: int = 128, group=None, store: str = "peer"):
+        """store: "peer" -- the epilogue TMA-stores each tile into every rank's
+        buffer (CUDA IPC mappings), once per rank; "nvls" -- it stores each
+        tile once through the NVSwitch's multicast (kc_gemm_w4a16_allgather_mc
+        on a symmetric buffer), which writes it into every rank's copy
+        (RuntimeError where the platform has no multicast)."""
+        if store not in ("peer", "nvls"):
+            raise ValueError("store must be 'peer' or 'nvls'")
+        self.store = store
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.M, self.N, self.K, self.gs = M, N, K, group_size
         self.n_shard = N // self.world
         shard_range(N, self.world, self.rank)  # validates the split
+        self.barrier = PeerBarrier(group)
+        if store == "nvls":
+            self.symm = SymmetricBuffer((M, N), torch.bfloat16, group)
+            self.out = self.symm.local
+            return
         self.out_bufs = PeerBuffers(M * N * 2, group)
         self.out = self.out_bufs.local((M, N), torch.bfloat16)
         self._outs = (ctypes.c_void_p * self.world)(*self.out_bufs.ptrs)
-        self.barrier = PeerBarrier(group)
 
     def launch(self, x: torch.Tensor, packed_shard: torch.Tensor, scales_shard: torch.Tensor) -> None:
         """The fused GEMM alone (no barrier): for timing and for callers that
         synchronize the ranks themselves."""
         check_col_parallel_w4a16(self.M, self.K, self.n_shard, self.gs, x, packed_shard, scales_shard)
+        if self.store == "nvls":
+            check(lib().kc_gemm_w4a16_allgather_mc(
+                ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(packed_shard.data_ptr()),
+                ctypes.c_void_p(scales_shard.data_ptr()), ctypes.c_void_p(self.symm.multicast_ptr),
+                self.world, self.rank, self.M, self.n_shard, self.K, self.gs, _stream()))
+            return
         check(lib().kc_gemm_w4a16_allgather(
             ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(packed_shard.data_ptr()),
             ctypes.c_void_p(scales_shard.data_ptr()), self._outs, self.world, self.rank, self.M,
@@ -312,6 +330,9 @@ class ColParallelW4A16:
     def close(self) -> None:
         torch.cuda.synchronize()
         self.barrier.close()
+        if self.store == "nvls":
+            self.symm.close()
+            return
         self.out_bufs.close()
 
 
@@ -327,8 +348,8 @@ class RowParallelFP8:
 
     def __init__(self, M: int, N: int, group=None, reduce: str = "peer", chunks: int = 4,
                  comm_sms: int = 16):
-        if reduce not in ("peer", "nccl", "overlap", "nvls"):
-            raise ValueError("reduce must be 'peer', 'nccl', 'overlap' or 'nvls'")
+        if reduce not in ("peer", "nccl", "overlap", "nvls", "fused"):
+            raise ValueError("reduce must be 'peer', 'nccl', 'overlap', 'nvls' or 'fused'")
         self.chunks, self.comm_sms = chunks, comm_sms
         self.reduce = reduce
         self.group = group
@@ -338,6 +359,24 @@ class RowParallelFP8:
         if (M * N) % (8 * self.world):
             raise ValueError("M * N must be a multiple of 8 * world")
         self.barrier = PeerBarrier(group)
+        if reduce == "fused":
+            # kc_gemm_fp8_allreduce: the sum in the GEMM's epilogue
+            R = self.world
+            if R < 2 or M % (128 * R) or N % 256:
+                raise ValueError("the fused sum needs 2+ ranks, M % (128 * ranks) == 0 and N % 256 == 0")
+            per = (M // 128 // R) * (N // 256)
+            self.out_bufs = PeerBuffers(M * N * 2, group)
+            self.recv_bufs = PeerBuffers((R - 1) * (M // R) * N * 2, group)
+            self.flag_bufs = PeerBuffers((R - 1) * per * 4, group)
+            self.flag_bufs.local(((R - 1) * per,), torch.int32).zero_()
+            torch.cuda.synchronize()
+            dist.barrier(group=group)          # every flag array is zero before first use
+            self.out = self.out_bufs.local((M, N), torch.bfloat16)
+            self._outs = (ctypes.c_void_p * R)(*self.out_bufs.ptrs)
+            self._recvs = (ctypes.c_void_p * R)(*self.recv_bufs.ptrs)
+            self._flags = (ctypes.c_void_p * R)(*self.flag_bufs.ptrs)
+            self.epoch = 0
+            return
         if reduce == "nvls":
             # one symmetric bf16 buffer: the GEMM writes this rank's partial
             # into its own copy, the switch sums the copies in place
@@ -367,6 +406,18 @@ class RowParallelFP8:
                                             self.chunks, self.comm_sms, self.group)
         if self.reduce == "nvls":
             return self._nvls(a_codes_shard, sa, w_codes_shard, sw, Kr, entry_barrier)
+        if self.reduce == "fused":
+            # the ranks' GEMMs start together (the flag waits are bounded), and
+            # every sum is in every output after the exit barrier
+            self.barrier()
+            self.epoch += 1
+            check(l.kc_gemm_fp8_allreduce(
+                ctypes.c_void_p(a_codes_shard.data_ptr()), ctypes.c_void_p(sa.data_ptr()),
+                ctypes.c_void_p(w_codes_shard.data_ptr()), ctypes.c_void_p(sw.data_ptr()),
+                self._outs, self._recvs, self._flags, self.world, self.rank, self.epoch, self.M,
+                self.N, Kr, self.barrier.timeout_ns, _stream()))
+            self.barrier()
+            return self.out
         if entry_barrier:
             self.barrier()
         check(l.kc_gemm_fp8(ctypes.c_void_p(a_codes_shard.data_ptr()), ctypes.c_void_p(sa.data_ptr()),
@@ -422,6 +473,11 @@ class RowParallelFP8:
         self.barrier.close()
         if self.reduce == "nvls":
             self.symm.close()
+            return
+        if self.reduce == "fused":
+            self.out_bufs.close()
+            self.recv_bufs.close()
+            self.flag_bufs.close()
             return
         self.part_bufs.close()
         self.out_bufs.close()

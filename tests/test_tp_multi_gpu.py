@@ -1,14 +1,17 @@
 """Multi-GPU: the tensor-parallel drivers on 2 GPUs (one process per GPU, NCCL).
 
-Column parallel: the fused GEMM + all-gather (kc_gemm_w4a16_allgather) must
-give every rank the single-GPU kc_gemm_w4a16 result of the full problem bit
-for bit (each output tile is computed by one rank with the same arithmetic and
+Column parallel: the fused GEMM + all-gather (kc_gemm_w4a16_allgather, and
+kc_gemm_w4a16_allgather_mc through the switch's multicast where available)
+must give every rank the single-GPU kc_gemm_w4a16 result of the full problem
+bit for bit (each output tile is computed by one rank with the same arithmetic and
 stored, unchanged, into every rank's buffer).  Row parallel: the K-sharded FP8
 GEMM + bf16 sum -- by NCCL all-reduce (also row block by row block, each
 block's all-reduce overlapping the next block's GEMM) and by the peer-memory kernel
 kc_allreduce_bf16_peer -- against the single-GPU FP8 GEMM, normwise <= 1e-2
 (bf16 partials are rounded before the sum); the peer sum is identical on
-every rank; so is the in-switch sum (RowParallelFP8 reduce="nvls":
+every rank; so are the sum fused into the GEMM epilogue
+(kc_gemm_fp8_allreduce: partial tiles to their row owner, the owner's bf16
+sum to every rank) and the in-switch sum (RowParallelFP8 reduce="nvls":
 multimem.ld_reduce / multimem.st through NVLink SHARP, where the platform has
 multicast).  MLP block (tp.MLPBlockW4A16, the reference's col-parallel ->
 GELU -> row-parallel chain): the sharded block against the two unsharded
@@ -59,6 +62,17 @@ def _rank_main(rank, world, port, out_dir):
         y = col(x, packed[n0:n1].contiguous(), scales[n0:n1].contiguous())
         torch.cuda.synchronize()
         col_ok = bool(torch.equal(y.view(torch.int16), full.view(torch.int16)))
+        # the same through the switch's multicast (one store per tile), where available
+        try:
+            colm = tp.ColParallelW4A16(M, N, K, gs, store="nvls")
+        except RuntimeError:
+            colm = None
+        if colm is not None:
+            for _ in range(2):
+                ym = colm(x, packed[n0:n1].contiguous(), scales[n0:n1].contiguous())
+            torch.cuda.synchronize()
+            col_ok = col_ok and bool(torch.equal(ym.view(torch.int16), full.view(torch.int16)))
+            colm.close()
 
         # row parallel FP8
         M2, N2, K2 = 256, 512, 2048
@@ -91,6 +105,19 @@ def _rank_main(rank, world, port, out_dir):
         dist.all_gather(gathered, y2.clone())
         row_same = all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16)) for g in gathered)
         rp.close()
+        # the sum fused into the GEMM epilogue (partials to their row owner, the
+        # owner's sum to every rank), twice: the second call reuses the buffers
+        # and flags with the next epoch
+        rf = tp.RowParallelFP8(M2, N2, reduce="fused")
+        rf(qa_s, sa, qw_s, sw)
+        y5 = rf(qa_s, sa, qw_s, sw).clone()
+        torch.cuda.synchronize()
+        fused_err = float((y5.float() - ref).abs().max() / ref.abs().max())
+        gathered = [torch.empty_like(y5) for _ in range(world)]
+        dist.all_gather(gathered, y5)
+        fused_same = float(all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16))
+                               for g in gathered))
+        rf.close()
         # the in-switch sum (NVLink SHARP multicast), two row blocks, twice in a
         # row (the second call reuses the symmetric buffer behind the barriers)
         try:
@@ -129,8 +156,8 @@ def _rank_main(rank, world, port, out_dir):
         mlp_err = float((y3 - y_full).abs().max() / y_full.abs().max())
         status = l.kc_get_device_status()
         np.save(os.path.join(out_dir, f"rank{rank}.npy"),
-                np.array([col_ok, row_err, status, row_same, mlp_err, nvls_err, nvls_same],
-                         dtype=np.float64))
+                np.array([col_ok, row_err, status, row_same, mlp_err, nvls_err, nvls_same,
+                          fused_err, fused_same], dtype=np.float64))
         col.close()
     finally:
         dist.destroy_process_group()
@@ -142,11 +169,14 @@ def test_tensor_parallel_two_gpus(tmp_path):
     import torch.multiprocessing as mp
     mp.spawn(_rank_main, args=(WORLD, _free_port(), str(tmp_path)), nprocs=WORLD, join=True)
     for r in range(WORLD):
-        col_ok, row_err, status, row_same, mlp_err, nvls_err, nvls_same = np.load(tmp_path / f"rank{r}.npy")
+        (col_ok, row_err, status, row_same, mlp_err, nvls_err, nvls_same, fused_err,
+         fused_same) = np.load(tmp_path / f"rank{r}.npy")
         assert row_same == 1.0, "peer all-reduce outputs differ between ranks"
         assert col_ok == 1.0, f"rank {r}: gathered W4A16 output differs from the single-GPU GEMM"
         assert row_err <= 1e-2, f"rank {r}: row-parallel FP8 error {row_err}"
         assert mlp_err <= 1e-5, f"rank {r}: MLP block error {mlp_err}"
+        assert fused_err <= 1e-2, f"rank {r}: row-parallel FP8 (sum in the epilogue) error {fused_err}"
+        assert fused_same == 1.0, "epilogue-sum outputs differ between ranks"
         if nvls_err >= 0:
             assert nvls_err <= 1e-2, f"rank {r}: row-parallel FP8 (in-switch sum) error {nvls_err}"
             assert nvls_same == 1.0, "in-switch sum outputs differ between ranks"

@@ -677,6 +677,9 @@ class GemmFP8(Workload):
                            f"block's GEMM (GEMM on all but {self.rp.comm_sms} SMs)"),
                "peer": ("kc_allreduce_bf16_peer over NVLink peer memory (each GPU reduces 1/N of the "
                         "output in fp32 and writes it to every GPU) between two peer-flag barriers"),
+               "fused": ("the GEMM epilogue itself (kc_gemm_fp8_allreduce: each partial tile written "
+                         "over NVLink into the receive slot of the rank owning its rows, the owner's "
+                         "bf16 sum written into every rank's output), between two peer-flag barriers"),
                "nvls": (f"the NVSwitch in place (kc_allreduce_bf16_nvls: multimem.ld_reduce with fp32 "
                         f"accumulation + multimem.st on a symmetric buffer) for {self.rp.chunks} row "
                         f"blocks, each behind a peer-flag barrier and under the next block's GEMM "

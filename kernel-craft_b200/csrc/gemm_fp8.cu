@@ -43,8 +43,12 @@ constexpr uint32_t kTmemCols = 512;
 // to its fp32 accumulator and writes the bf16 sum into every rank's output.
 // Per GPU that sends (R-1)/R of the output as partials and (R-1)/R as sums,
 // both under the MMAs of the following tiles.
+// Tiles travel as eight 128-row x 32-column chunks, each staged in shared
+// memory and written with one TMA store per destination (large NVLink writes
+// instead of per-thread 16-byte stores).
 struct RsParams {
-    __nv_bfloat16* outs[KC_MAX_RANKS];   // every rank's [M, N] bf16 output (pitch N)
+    CUtensorMap out_map[KC_MAX_RANKS];   // every rank's output bf16 {N, M}, box {32, 128}
+    CUtensorMap recv_map[KC_MAX_RANKS];  // every rank's receive slots bf16 {N, (R-1) M/R}, box {32, 128}
     __nv_bfloat16* recv[KC_MAX_RANKS];   // every rank's receive slots: (R - 1) x [M / R, N] bf16
     int* flags[KC_MAX_RANKS];            // every rank's flags: (R - 1) x tiles per owner block
     int nranks, rank, epoch;
@@ -85,6 +89,7 @@ __device__ __forceinline__ void tile_coords(const Params& P, int L, int& m0, int
 struct Smem {
     uint8_t a[kStages][kABytes];   // 1024-byte aligned (swizzle atoms)
     uint8_t b[kStages][kBBytes];
+    uint8_t stage[2][BM * 32 * 2]; // fused-sum epilogue: a 128 x 32 bf16 chunk, double-buffered
     uint64_t full[kStages];
     uint64_t empty[kStages];
     uint64_t tmem_full[2];
@@ -191,6 +196,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
         // -------------------------------- epilogue --------------------------------
         const int q = warp & 3;                      // TMEM lane quarter of this warp
         const int et = threadIdx.x - 64;             // 0..127 over the epilogue warps
+        // RS: the flag of the last partial tile, raised once that tile's stores
+        // have landed -- after the next tile's stores are issued, or before
+        // this thread waits for peers, or at the end; it is never held while
+        // this CTA waits for another rank, so no wait can close a cycle
+        int* pend_flag = nullptr;
+        auto raise_pending = [&]() {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            __threadfence_system();
+            asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(pend_flag), "r"(P.rs.epoch) : "memory");
+            pend_flag = nullptr;
+        };
         uint32_t t = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
             const uint32_t acc = t & 1u;
@@ -207,6 +223,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
                 // (bounded; a peer that never delivers makes the tile NaN)
                 if (mine) {
                     if (et == 0) {
+                        if (pend_flag) {   // nothing of ours is held while we wait
+                            sm100::bulk_wait_group0();
+                            raise_pending();
+                        }
                         const int per = (P.tiles_m / P.rs.nranks) * P.tiles_n;
                         const uint64_t t0 = sm100::globaltimer();
                         for (int sl = 0; sl < P.rs.nranks - 1 && peers_ok; ++sl) {
@@ -238,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
                 sm100::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + acc * BN + c * 32, r);
                 sm100::tmem_wait_ld();
                 const int nb = n0 + c * 32;
-                if (m >= P.M || nb >= P.N) continue;
+                if (!RS && (m >= P.M || nb >= P.N)) continue;   // RS tiles are always whole
                 const float4* swv = reinterpret_cast<const float4*>(P.sw + nb);
                 float v[32];
 #pragma unroll
@@ -252,52 +272,50 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
                 }
                 if constexpr (RS) {
                     const int R = P.rs.nranks, rows = P.M / R;
-                    if (!mine) {
-                        // this rank's partial into the owner's receive slot
-                        const int sl = (P.rs.rank - owner - 1 + R) % R;
-                        __nv_bfloat16* o = P.rs.recv[owner] + ((size_t)sl * rows + (m - owner * rows)) * P.N + nb;
-                        if (poison)
+                    if (mine) {
+                        // the owner: add the peers' partials (slots in order)
+                        for (int sl = 0; sl < R - 1; ++sl) {
+                            const uint4* in = reinterpret_cast<const uint4*>(
+                                P.rs.recv[P.rs.rank] + ((size_t)sl * rows + (m - P.rs.rank * rows)) * P.N + nb);
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7FC00000);
+                            for (int i = 0; i < 4; ++i) {
+                                const uint4 w = __ldcg(in + i);
+                                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            reinterpret_cast<uint4*>(o)[i] =
-                                make_uint4(bf16x2_bits(v[8 * i], v[8 * i + 1]),
-                                           bf16x2_bits(v[8 * i + 2], v[8 * i + 3]),
-                                           bf16x2_bits(v[8 * i + 4], v[8 * i + 5]),
-                                           bf16x2_bits(v[8 * i + 6], v[8 * i + 7]));
-                        continue;
-                    }
-                    // the owner: add the peers' partials (slots in order), then
-                    // the sum into every rank's output
-                    for (int sl = 0; sl < R - 1; ++sl) {
-                        const uint4* in = reinterpret_cast<const uint4*>(
-                            P.rs.recv[P.rs.rank] + ((size_t)sl * rows + (m - P.rs.rank * rows)) * P.N + nb);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const uint4 w = __ldcg(in + i);
-                            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                v[8 * i + 2 * e] += __uint_as_float(ww[e] << 16);
-                                v[8 * i + 2 * e + 1] += __uint_as_float(ww[e] & 0xFFFF0000u);
+                                for (int e = 0; e < 4; ++e) {
+                                    v[8 * i + 2 * e] += __uint_as_float(ww[e] << 16);
+                                    v[8 * i + 2 * e + 1] += __uint_as_float(ww[e] & 0xFFFF0000u);
+                                }
                             }
                         }
                     }
                     if (poison)
 #pragma unroll
                         for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7FC00000);
-                    uint4 o4[4];
+                    // stage the chunk (the tile's row q * 32 + lane, this thread's
+                    // TMEM lane: 64 bytes), then one TMA store per
+                    // destination: the owner's receive slot for a partial, every
+                    // rank's output for a sum
+                    const int buf = c & 1;
+                    if (et == 0) sm100::bulk_wait_group_read1();   // this buffer's last stores read it
+                    sm100::named_sync(1, 128);
+                    uint4* st4 = reinterpret_cast<uint4*>(S.stage[buf] + (q * 32 + lane) * 64);
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
-                        o4[i] = make_uint4(bf16x2_bits(v[8 * i], v[8 * i + 1]), bf16x2_bits(v[8 * i + 2], v[8 * i + 3]),
-                                           bf16x2_bits(v[8 * i + 4], v[8 * i + 5]),
-                                           bf16x2_bits(v[8 * i + 6], v[8 * i + 7]));
-                    for (int d = 0; d < R; ++d) {
-                        const int r = (P.rs.rank + d) % R;   // own copy first
-                        uint4* o = reinterpret_cast<uint4*>(P.rs.outs[r] + (size_t)m * P.N + nb);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) o[i] = o4[i];
+                        st4[i] = make_uint4(bf16x2_bits(v[8 * i], v[8 * i + 1]), bf16x2_bits(v[8 * i + 2], v[8 * i + 3]),
+                                            bf16x2_bits(v[8 * i + 4], v[8 * i + 5]),
+                                            bf16x2_bits(v[8 * i + 6], v[8 * i + 7]));
+                    sm100::fence_proxy_async_smem();
+                    sm100::named_sync(1, 128);
+                    if (et == 0) {
+                        if (!mine) {
+                            const int sl = (P.rs.rank - owner - 1 + R) % R;
+                            sm100::tma_store_2d(&P.rs.recv_map[owner], S.stage[buf], nb, sl * rows + (m0 - owner * rows));
+                        } else {
+                            for (int d = 0; d < R; ++d)   // own copy first
+                                sm100::tma_store_2d(&P.rs.out_map[(P.rs.rank + d) % R], S.stage[buf], nb, m0);
+                        }
+                        sm100::bulk_commit_group();
                     }
                     continue;
                 }
@@ -333,20 +351,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(&S.tmem_empty[acc]);
             if constexpr (RS) {
-                // a partial for another owner: every thread's stores, then the flag
-                if (!mine) {
-                    __threadfence_system();
-                    sm100::named_sync(1, 128);
-                    if (et == 0) {
+                if (et == 0) {
+                    // the previous partial tile's flag: its groups are all but this
+                    // tile's BN / 32 newest
+                    if (pend_flag) {
+                        sm100::bulk_wait_group<BN / 32>();
+                        raise_pending();
+                    }
+                    if (!mine) {
                         const int R = P.rs.nranks, per = (P.tiles_m / R) * P.tiles_n;
                         const int sl = (P.rs.rank - owner - 1 + R) % R;
-                        int* f = P.rs.flags[owner] + sl * per + j;
-                        asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(f), "r"(P.rs.epoch) : "memory");
+                        pend_flag = P.rs.flags[owner] + sl * per + j;
                     }
                 }
             }
         }
-        if constexpr (RS) __threadfence_system();   // the sums, before the barrier after the kernel
+        if constexpr (RS) {   // the sums and the last flag, before the barrier after the kernel
+            if (et == 0) {
+                sm100::bulk_wait_group0();
+                if (pend_flag) raise_pending();
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+            __threadfence_system();
+        }
     }
 
     // teardown: every MMA has been consumed by the epilogue before this barrier
@@ -423,9 +450,15 @@ int kc_gemm_fp8_allreduce(const int8_t* a_codes_shard, const float* sa, const in
         KC_REQUIRE(outs[r] && recvs[r] && flags[r] && kc::aligned(outs[r], 16) && kc::aligned(recvs[r], 16) &&
                        kc::aligned(flags[r], 4),
                    KC_ERR_ALIGNMENT, "buffers of rank %d null or misaligned", r);
-        P.rs.outs[r] = static_cast<__nv_bfloat16*>(outs[r]);
         P.rs.recv[r] = static_cast<__nv_bfloat16*>(recvs[r]);
         P.rs.flags[r] = flags[r];
+        int e = kc::encode_2d(&P.rs.out_map[r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, outs[r], (uint64_t)N,
+                              (uint64_t)M, (uint64_t)N * 2, 32, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (e) return e;
+        e = kc::encode_2d(&P.rs.recv_map[r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, recvs[r], (uint64_t)N,
+                          (uint64_t)(nranks - 1) * (M / nranks), (uint64_t)N * 2, 32, BM,
+                          CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (e) return e;
     }
     P.rs.nranks = nranks;
     P.rs.rank = rank;

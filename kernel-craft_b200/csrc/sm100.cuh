@@ -155,9 +155,18 @@ __device__ __forceinline__ void bulk_commit_group() {
 __device__ __forceinline__ void bulk_wait_group_read0() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// ... leaving at most the newest group still reading ...
+__device__ __forceinline__ void bulk_wait_group_read1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // ... or has completed entirely (writes visible in global memory).
 __device__ __forceinline__ void bulk_wait_group0() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// ... all but the N newest groups have completed entirely.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (TMA) reads of them.

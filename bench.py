@@ -623,11 +623,12 @@ class GemmFP8(Workload):
         self.rp = None
         if world > 1:
             import tp
-            # measured on 2 B200s: an NCCL all-reduce after the whole GEMM beats
-            # the in-switch sum there (it moves 1.5x the bytes of a ring at
-            # 2 ranks, (1 + 1/N)x the output at N) and beats splitting the GEMM
-            # into blocks; from 4 ranks on the in-switch sum moves fewer bytes
-            reduce = os.environ.get("KC_TP_REDUCE", "nccl" if world == 2 else "nvls")
+            # measured on 2 B200s (whole-GEMM TFLOP/s): the sum fused into the
+            # GEMM epilogue 2726, NCCL after the GEMM 2018, the in-switch sum
+            # 1771 (it moves 1.5x a ring's bytes at 2 ranks, (1 + 1/N)x the
+            # output at N ranks, where the fused sum moves 2(N-1)/N x); from 4
+            # ranks on the in-switch sum moves the fewest bytes
+            reduce = os.environ.get("KC_TP_REDUCE", "fused" if world == 2 else "nvls")
             kw = dict(chunks=int(os.environ.get("KC_TP_CHUNKS", "4")),
                       comm_sms=int(os.environ.get("KC_TP_COMM_SMS", "16")))
             try:

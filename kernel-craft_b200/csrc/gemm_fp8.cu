@@ -43,12 +43,12 @@ constexpr uint32_t kTmemCols = 512;
 // to its fp32 accumulator and writes the bf16 sum into every rank's output.
 // Per GPU that sends (R-1)/R of the output as partials and (R-1)/R as sums,
 // both under the MMAs of the following tiles.
-// Tiles travel as eight 128-row x 32-column chunks, each staged in shared
-// memory and written with one TMA store per destination (large NVLink writes
-// instead of per-thread 16-byte stores).
+// Tiles travel as four 128-row x 64-column pieces (two TMEM chunks each),
+// each staged in shared memory and written with one TMA store per
+// destination: 128-byte rows over NVLink instead of per-thread 16-byte stores.
 struct RsParams {
-    CUtensorMap out_map[KC_MAX_RANKS];   // every rank's output bf16 {N, M}, box {32, 128}
-    CUtensorMap recv_map[KC_MAX_RANKS];  // every rank's receive slots bf16 {N, (R-1) M/R}, box {32, 128}
+    CUtensorMap out_map[KC_MAX_RANKS];   // every rank's output bf16 {N, M}, box {64, 128}
+    CUtensorMap recv_map[KC_MAX_RANKS];  // every rank's receive slots bf16 {N, (R-1) M/R}, box {64, 128}
     __nv_bfloat16* recv[KC_MAX_RANKS];   // every rank's receive slots: (R - 1) x [M / R, N] bf16
     int* flags[KC_MAX_RANKS];            // every rank's flags: (R - 1) x tiles per owner block
     int nranks, rank, epoch;
@@ -89,7 +89,7 @@ __device__ __forceinline__ void tile_coords(const Params& P, int L, int& m0, int
 struct Smem {
     uint8_t a[kStages][kABytes];   // 1024-byte aligned (swizzle atoms)
     uint8_t b[kStages][kBBytes];
-    uint8_t stage[2][BM * 32 * 2]; // fused-sum epilogue: a 128 x 32 bf16 chunk, double-buffered
+    uint8_t stage[2][BM * 64 * 2]; // fused-sum epilogue: a 128 x 64 bf16 piece, double-buffered
     uint64_t full[kStages];
     uint64_t empty[kStages];
     uint64_t tmem_full[2];
@@ -296,26 +296,32 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
                     // TMEM lane: 64 bytes), then one TMA store per
                     // destination: the owner's receive slot for a partial, every
                     // rank's output for a sum
-                    const int buf = c & 1;
-                    if (et == 0) sm100::bulk_wait_group_read1();   // this buffer's last stores read it
-                    sm100::named_sync(1, 128);
-                    uint4* st4 = reinterpret_cast<uint4*>(S.stage[buf] + (q * 32 + lane) * 64);
+                    // chunks 2p and 2p + 1 fill the halves of buffer p & 1
+                    const int buf = (c >> 1) & 1, half = c & 1;
+                    if (half == 0) {
+                        if (et == 0) sm100::bulk_wait_group_read1();   // this buffer's last stores read it
+                        sm100::named_sync(1, 128);
+                    }
+                    uint4* st4 = reinterpret_cast<uint4*>(S.stage[buf] + (q * 32 + lane) * 128 + half * 64);
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
                         st4[i] = make_uint4(bf16x2_bits(v[8 * i], v[8 * i + 1]), bf16x2_bits(v[8 * i + 2], v[8 * i + 3]),
                                             bf16x2_bits(v[8 * i + 4], v[8 * i + 5]),
                                             bf16x2_bits(v[8 * i + 6], v[8 * i + 7]));
-                    sm100::fence_proxy_async_smem();
-                    sm100::named_sync(1, 128);
-                    if (et == 0) {
-                        if (!mine) {
-                            const int sl = (P.rs.rank - owner - 1 + R) % R;
-                            sm100::tma_store_2d(&P.rs.recv_map[owner], S.stage[buf], nb, sl * rows + (m0 - owner * rows));
-                        } else {
-                            for (int d = 0; d < R; ++d)   // own copy first
-                                sm100::tma_store_2d(&P.rs.out_map[(P.rs.rank + d) % R], S.stage[buf], nb, m0);
+                    if (half == 1) {
+                        sm100::fence_proxy_async_smem();
+                        sm100::named_sync(1, 128);
+                        if (et == 0) {
+                            const int x = nb - 32;
+                            if (!mine) {
+                                const int sl = (P.rs.rank - owner - 1 + R) % R;
+                                sm100::tma_store_2d(&P.rs.recv_map[owner], S.stage[buf], x, sl * rows + (m0 - owner * rows));
+                            } else {
+                                for (int d = 0; d < R; ++d)   // own copy first
+                                    sm100::tma_store_2d(&P.rs.out_map[(P.rs.rank + d) % R], S.stage[buf], x, m0);
+                            }
+                            sm100::bulk_commit_group();
                         }
-                        sm100::bulk_commit_group();
                     }
                     continue;
                 }
@@ -353,9 +359,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
             if constexpr (RS) {
                 if (et == 0) {
                     // the previous partial tile's flag: its groups are all but this
-                    // tile's BN / 32 newest
+                    // tile's BN / 64 newest
                     if (pend_flag) {
-                        sm100::bulk_wait_group<BN / 32>();
+                        sm100::bulk_wait_group<BN / 64>();
                         raise_pending();
                     }
                     if (!mine) {
@@ -453,10 +459,10 @@ int kc_gemm_fp8_allreduce(const int8_t* a_codes_shard, const float* sa, const in
         P.rs.recv[r] = static_cast<__nv_bfloat16*>(recvs[r]);
         P.rs.flags[r] = flags[r];
         int e = kc::encode_2d(&P.rs.out_map[r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, outs[r], (uint64_t)N,
-                              (uint64_t)M, (uint64_t)N * 2, 32, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+                              (uint64_t)M, (uint64_t)N * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (e) return e;
         e = kc::encode_2d(&P.rs.recv_map[r], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, recvs[r], (uint64_t)N,
-                          (uint64_t)(nranks - 1) * (M / nranks), (uint64_t)N * 2, 32, BM,
+                          (uint64_t)(nranks - 1) * (M / nranks), (uint64_t)N * 2, 64, BM,
                           CU_TENSOR_MAP_SWIZZLE_NONE);
         if (e) return e;
     }

@@ -337,14 +337,18 @@ class ColParallelW4A16:
 
 
 class RowParallelFP8:
-    """Row-parallel FP8 linear with the sum done over NVLink peer memory.
+    """Row-parallel FP8 linear: each rank's K-shard partial, summed in bf16
+    into every rank's [M, N] output.
 
     Every rank holds its K shard of the activation and weight codes and the
-    full-row scales; ``__call__`` runs kc_gemm_fp8 into this rank's shared
-    bf16 partial buffer, then kc_allreduce_bf16_peer (each rank reduces its
-    1/R slice from all partials in fp32 and writes it into every rank's
-    output), with a peer-memory barrier before and after the reduction.
-    Returns this rank's [M, N] bf16 output buffer (the same on every rank)."""
+    full-row scales; ``__call__`` returns this rank's [M, N] bf16 output
+    buffer (the same on every rank).  ``reduce`` picks the sum:
+    "fused" -- kc_gemm_fp8_allreduce, the sum inside the GEMM's epilogue
+    (partial tiles to the rank owning their rows over NVLink, the owner's sum
+    to every rank), between two peer barriers; "nvls" -- kc_allreduce_bf16_nvls
+    in the NVSwitch per row block under the next block's GEMM; "peer" --
+    kc_gemm_fp8 then kc_allreduce_bf16_peer between peer barriers; "nccl" --
+    one NCCL all-reduce; "overlap" -- NCCL per row block."""
 
     def __init__(self, M: int, N: int, group=None, reduce: str = "peer", chunks: int = 4,
                  comm_sms: int = 16):

@@ -623,12 +623,10 @@ class GemmFP8(Workload):
         self.rp = None
         if world > 1:
             import tp
-            # measured on 2 B200s (whole-GEMM TFLOP/s): the sum fused into the
-            # GEMM epilogue 2726, NCCL after the GEMM 2018, the in-switch sum
-            # 1771 (it moves 1.5x a ring's bytes at 2 ranks, (1 + 1/N)x the
-            # output at N ranks, where the fused sum moves 2(N-1)/N x); from 4
-            # ranks on the in-switch sum moves the fewest bytes
-            reduce = os.environ.get("KC_TP_REDUCE", "fused" if world == 2 else "nvls")
+            # measured (whole-GEMM TFLOP/s; one GPU 2175): the sum fused into
+            # the GEMM epilogue 2726 on 2 B200s and 2257 on 4; NCCL after the
+            # GEMM 2018 / 2023; the in-switch sum per row block 1771 / 1951
+            reduce = os.environ.get("KC_TP_REDUCE", "fused")
             kw = dict(chunks=int(os.environ.get("KC_TP_CHUNKS", "4")),
                       comm_sms=int(os.environ.get("KC_TP_COMM_SMS", "16")))
             try:
@@ -745,7 +743,8 @@ class GemmFP8(Workload):
             return True, None
         torch = self.torch
         import tp
-        M, N, K = 256, 512, 512 * self.world
+        # M: two 128-row tiles per rank (the fused sum owns rows in R blocks)
+        M, N, K = 256 * self.world, 512, 512 * self.world
         g = torch.Generator(device=self.dev)
         g.manual_seed(4322)
         x = torch.randn(M, K, device=self.dev, generator=g)
@@ -762,7 +761,7 @@ class GemmFP8(Workload):
         chk(l.kc_gemm_fp8(qa.data_ptr(), sa.data_ptr(), qw.data_ptr(), sw.data_ptr(), ref.data_ptr(),
                           1, M, N, K, N, self.s_ptr))
         k0, k1 = tp.shard_range(K, self.world, self.rank)
-        rp = tp.RowParallelFP8(M, N, reduce=self.rp.reduce)
+        rp = tp.RowParallelFP8(M, N, reduce=self.rp.reduce, chunks=self.rp.chunks, comm_sms=self.rp.comm_sms)
         out = rp(qa[:, k0:k1].contiguous(), sa, qw[:, k0:k1].contiguous(), sw).clone()
         torch.cuda.synchronize()
         rp.close()

@@ -679,6 +679,10 @@ class GemmFP8(Workload):
                "fused": ("the GEMM epilogue itself (kc_gemm_fp8_allreduce: each partial tile written "
                          "over NVLink into the receive slot of the rank owning its rows, the owner's "
                          "bf16 sum written into every rank's output), between two peer-flag barriers"),
+               "fused_nvls": ("the GEMM epilogue itself with the NVSwitch (kc_gemm_fp8_allreduce_mc: "
+                              "each partial tile into this rank's copy of a symmetric buffer, the "
+                              "owner's multimem.ld_reduce + multimem.st into every copy), between two "
+                              "peer-flag barriers"),
                "nvls": (f"the NVSwitch in place (kc_allreduce_bf16_nvls: multimem.ld_reduce with fp32 "
                         f"accumulation + multimem.st on a symmetric buffer) for {self.rp.chunks} row "
                         f"blocks, each behind a peer-flag barrier and under the next block's GEMM "

@@ -389,6 +389,20 @@ KC_API int kc_gemm_fp8_allreduce(const int8_t* a_codes_shard, const float* sa, c
                                  int nranks, int rank, int epoch, int M, int N, int K_shard,
                                  uint64_t timeout_ns, cudaStream_t stream);
 
+/* As kc_gemm_fp8_allreduce, with the sum done in the NVSwitch: every rank
+ * writes its partial tiles into its own copy `part` ([M, N] bf16) of a
+ * symmetric buffer whose multicast address is `mc_part`, and flags each tile
+ * to its owner; the owner sums the copies with multimem.ld_reduce (fp32
+ * accumulation) and writes the bf16 sum into every copy with multimem.st, so
+ * every rank's `part` ends as the full [M, N] result.  Per GPU the output
+ * crosses NVLink once outward and (1 + 1/nranks) times inward, where the
+ * peer form moves 2 (nranks - 1) / nranks each way.  flags, epoch, timeout,
+ * alignment of the launches and shape limits as for kc_gemm_fp8_allreduce. */
+KC_API int kc_gemm_fp8_allreduce_mc(const int8_t* a_codes_shard, const float* sa, const int8_t* w_codes_shard,
+                                    const float* sw, void* part, void* mc_part, int* const* flags, int nranks,
+                                    int rank, int epoch, int M, int N, int K_shard, uint64_t timeout_ns,
+                                    cudaStream_t stream);
+
 /* bf16 sum all-reduce over NVLink peer memory (one process per GPU; the
  * reference's counterpart is launch_ring_allreduce_nccl, fp32,
  * tensor_parallel_nccl.cu:105).  partials[r] / outs[r]: rank r's input and

@@ -53,6 +53,10 @@ struct RsParams {
     int* flags[KC_MAX_RANKS];            // every rank's flags: (R - 1) x tiles per owner block
     int nranks, rank, epoch;
     uint64_t timeout_ns;
+    // in-switch form (MC kernels): partials and sums in one symmetric buffer
+    CUtensorMap part_map;                // this rank's copy bf16 {N, M}, box {64, 128}
+    __nv_bfloat16* part;                 // this rank's copy [M, N]
+    uint8_t* mc_part;                    // its multicast address
 };
 
 struct alignas(64) Params {
@@ -104,7 +108,13 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <bool RS>
+// MC (with RS): every rank writes its partial tile into its own copy of a
+// symmetric buffer and flags the tile's owner; the owner writes its own
+// partial there too, then sums the R copies in the NVSwitch
+// (multimem.ld_reduce, fp32 accumulation) and stores the bf16 sum into every
+// copy (multimem.st).  Per GPU that moves the output once out and
+// (1 + 1/R) times in, against 2(R - 1)/R each way for the peer form.
+template <bool RS, bool MC = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_constant__ Params P) {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled operand tiles
@@ -272,7 +282,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
                 }
                 if constexpr (RS) {
                     const int R = P.rs.nranks, rows = P.M / R;
-                    if (mine) {
+                    if constexpr (MC) {
+                        if (mine) {
+                            // the owner's partial into its own copy; the switch sums
+                            // the copies once the tile is complete (below)
+                            if (poison)
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0x7FC00000);
+                            uint4* o = reinterpret_cast<uint4*>(P.rs.part + (size_t)m * P.N + nb);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                o[i] = make_uint4(bf16x2_bits(v[8 * i], v[8 * i + 1]), bf16x2_bits(v[8 * i + 2], v[8 * i + 3]),
+                                                  bf16x2_bits(v[8 * i + 4], v[8 * i + 5]),
+                                                  bf16x2_bits(v[8 * i + 6], v[8 * i + 7]));
+                            continue;
+                        }
+                    } else if (mine) {
                         // the owner: add the peers' partials (slots in order)
                         for (int sl = 0; sl < R - 1; ++sl) {
                             const uint4* in = reinterpret_cast<const uint4*>(
@@ -313,7 +338,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
                         sm100::named_sync(1, 128);
                         if (et == 0) {
                             const int x = nb - 32;
-                            if (!mine) {
+                            if (MC) {   // a partial, into this rank's own copy
+                                sm100::tma_store_2d(&P.rs.part_map, S.stage[buf], x, m0);
+                            } else if (!mine) {
                                 const int sl = (P.rs.rank - owner - 1 + R) % R;
                                 sm100::tma_store_2d(&P.rs.recv_map[owner], S.stage[buf], x, sl * rows + (m0 - owner * rows));
                             } else {
@@ -356,6 +383,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_fp8_kernel(const __grid_cons
             sm100::tc_fence_before();
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(&S.tmem_empty[acc]);
+            if constexpr (MC) {
+                if (mine) {
+                    // every copy of the tile is complete: the switch sums them and
+                    // writes the sum into every copy (128 rows x 32 pieces of 16 B)
+                    __threadfence_system();
+                    sm100::named_sync(1, 128);
+                    uint8_t* base = P.rs.mc_part + ((size_t)m0 * P.N + n0) * 2;
+#pragma unroll 8
+                    for (int i = et; i < BM * (BN / 8); i += 128) {
+                        uint8_t* a = base + (size_t)(i >> 5) * P.N * 2 + (i & 31) * 16;
+                        uint32_t w0, w1, w2, w3;
+                        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+                                     : "=r"(w0), "=r"(w1), "=r"(w2), "=r"(w3)
+                                     : "l"(a)
+                                     : "memory");
+                        asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1,%2,%3,%4};"
+                                     ::"l"(a), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                                     : "memory");
+                    }
+                }
+            }
             if constexpr (RS) {
                 if (et == 0) {
                     // the previous partial tile's flag: its groups are all but this
@@ -498,6 +546,62 @@ int kc_gemm_fp8_allreduce(const int8_t* a_codes_shard, const float* sa, const in
 int kc_gemm_fp8(const int8_t* a_codes, const float* sa, const int8_t* w_codes, const float* sw,
                 void* out, int out_f32, int M, int N, int K, int ldc, cudaStream_t stream) {
     return kc_gemm_fp8_ctas(a_codes, sa, w_codes, sw, out, out_f32, M, N, K, ldc, 0, stream);
+}
+
+int kc_gemm_fp8_allreduce_mc(const int8_t* a_codes_shard, const float* sa, const int8_t* w_codes_shard,
+                             const float* sw, void* part, void* mc_part, int* const* flags, int nranks,
+                             int rank, int epoch, int M, int N, int K_shard, uint64_t timeout_ns,
+                             cudaStream_t stream) {
+    KC_REQUIRE(a_codes_shard && sa && w_codes_shard && sw && part && mc_part && flags, KC_ERR_INVALID_ARG,
+               "null pointer argument");
+    KC_REQUIRE(nranks >= 2 && nranks <= KC_MAX_RANKS && rank >= 0 && rank < nranks, KC_ERR_INVALID_ARG,
+               "rank %d of %d: 2..%d ranks", rank, nranks, KC_MAX_RANKS);
+    KC_REQUIRE(M > 0 && M % (BM * nranks) == 0, KC_ERR_INVALID_ARG,
+               "M=%d must be a positive multiple of %d x nranks", M, BM);
+    KC_REQUIRE(N > 0 && N % BN == 0, KC_ERR_INVALID_ARG, "N=%d must be a positive multiple of %d", N, BN);
+    KC_REQUIRE(K_shard > 0 && K_shard % 16 == 0, KC_ERR_INVALID_ARG,
+               "K_shard=%d must be a positive multiple of 16", K_shard);
+    KC_REQUIRE(timeout_ns <= KC_PEER_BARRIER_MAX_TIMEOUT_NS, KC_ERR_INVALID_ARG, "timeout above the maximum");
+    KC_REQUIRE(kc::aligned(a_codes_shard, 16) && kc::aligned(w_codes_shard, 16) && kc::aligned(sw, 16) &&
+                   kc::aligned(part, 16) && kc::aligned(mc_part, 16),
+               KC_ERR_ALIGNMENT, "operands must be 16-byte aligned");
+    Params P{};
+    for (int r = 0; r < nranks; ++r) {
+        KC_REQUIRE(flags[r] && kc::aligned(flags[r], 4), KC_ERR_ALIGNMENT, "flags of rank %d null or misaligned", r);
+        P.rs.flags[r] = flags[r];
+    }
+    P.rs.nranks = nranks;
+    P.rs.rank = rank;
+    P.rs.epoch = epoch;
+    P.rs.timeout_ns = timeout_ns ? timeout_ns : KC_PEER_BARRIER_DEFAULT_TIMEOUT_NS;
+    P.rs.part = static_cast<__nv_bfloat16*>(part);
+    P.rs.mc_part = static_cast<uint8_t*>(mc_part);
+    int st = kc::encode_2d(&P.rs.part_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, part, (uint64_t)N, (uint64_t)M,
+                           (uint64_t)N * 2, 64, BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    st = kc::encode_2d(&P.amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, a_codes_shard, (uint64_t)K_shard, (uint64_t)M,
+                       (uint64_t)K_shard, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = kc::encode_2d(&P.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_codes_shard, (uint64_t)K_shard, (uint64_t)N,
+                       (uint64_t)K_shard, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    P.sa = sa;
+    P.sw = sw;
+    P.out = part;
+    P.M = M;
+    P.N = N;
+    P.K = K_shard;
+    P.ldc = N;
+    P.out_f32 = 0;
+    P.tiles_m = M / BM;
+    P.tiles_n = N / BN;
+    const size_t smem = sizeof(Smem) + 1024;
+    KC_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem),
+                "gemm_fp8 shared-memory attribute");
+    const int tiles = P.tiles_m * P.tiles_n;
+    gemm_fp8_kernel<true, true><<<std::min(tiles, kc::sm_count()), kThreads, smem, stream>>>(P);
+    return kc::check_launch("gemm_fp8_allreduce_mc");
 }
 
 }  // extern "C"

@@ -107,6 +107,7 @@ _PROTOS = [
     ("kc_gemm_w4a16_allgather_mc", ci, [vp, vp, vp, vp, ci, ci, ci, ci, ci, ci, vp]),
     ("kc_allreduce_bf16_peer", ci, [ctypes.POINTER(vp), ctypes.POINTER(vp), ci, ci, cl, vp]),
     ("kc_allreduce_bf16_nvls", ci, [vp, ci, ci, cl, ci, vp]),
+    ("kc_gemm_fp8_allreduce_mc", ci, [vp, vp, vp, vp, vp, vp, ctypes.POINTER(vp), ci, ci, ci, ci, ci, ci, ctypes.c_uint64, vp]),
     ("kc_gemm_fp8_allreduce", ci, [vp, vp, vp, vp, ctypes.POINTER(vp), ctypes.POINTER(vp), ctypes.POINTER(vp), ci, ci, ci, ci, ci, ci, ctypes.c_uint64, vp]),
     ("kc_peer_barrier", ci, [ctypes.POINTER(vp), ci, ci, ci, ctypes.c_uint64, vp, vp]),
     ("kc_ipc_handle_bytes", ci, []),

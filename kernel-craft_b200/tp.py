@@ -345,15 +345,17 @@ class RowParallelFP8:
     buffer (the same on every rank).  ``reduce`` picks the sum:
     "fused" -- kc_gemm_fp8_allreduce, the sum inside the GEMM's epilogue
     (partial tiles to the rank owning their rows over NVLink, the owner's sum
-    to every rank), between two peer barriers; "nvls" -- kc_allreduce_bf16_nvls
+    to every rank), between two peer barriers; "fused_nvls" --
+    kc_gemm_fp8_allreduce_mc, the same with the owner summing the ranks'
+    copies in the NVSwitch (multimem) on a symmetric buffer; "nvls" -- kc_allreduce_bf16_nvls
     in the NVSwitch per row block under the next block's GEMM; "peer" --
     kc_gemm_fp8 then kc_allreduce_bf16_peer between peer barriers; "nccl" --
     one NCCL all-reduce; "overlap" -- NCCL per row block."""
 
     def __init__(self, M: int, N: int, group=None, reduce: str = "peer", chunks: int = 4,
                  comm_sms: int = 16):
-        if reduce not in ("peer", "nccl", "overlap", "nvls", "fused"):
-            raise ValueError("reduce must be 'peer', 'nccl', 'overlap', 'nvls' or 'fused'")
+        if reduce not in ("peer", "nccl", "overlap", "nvls", "fused", "fused_nvls"):
+            raise ValueError("reduce must be 'peer', 'nccl', 'overlap', 'nvls', 'fused' or 'fused_nvls'")
         self.chunks, self.comm_sms = chunks, comm_sms
         self.reduce = reduce
         self.group = group
@@ -363,23 +365,30 @@ class RowParallelFP8:
         if (M * N) % (8 * self.world):
             raise ValueError("M * N must be a multiple of 8 * world")
         self.barrier = PeerBarrier(group)
-        if reduce == "fused":
-            # kc_gemm_fp8_allreduce: the sum in the GEMM's epilogue
+        if reduce in ("fused", "fused_nvls"):
+            # kc_gemm_fp8_allreduce(_mc): the sum in the GEMM's epilogue
             R = self.world
             if R < 2 or M % (128 * R) or N % 256:
                 raise ValueError("the fused sum needs 2+ ranks, M % (128 * ranks) == 0 and N % 256 == 0")
             per = (M // 128 // R) * (N // 256)
+            self.flag_bufs = PeerBuffers((R - 1) * per * 4, group)
+            self._flags = (ctypes.c_void_p * R)(*self.flag_bufs.ptrs)
+            self.epoch = 0
+            if reduce == "fused_nvls":
+                self.symm = SymmetricBuffer((M, N), torch.bfloat16, group)
+                self.out = self.symm.local
+                self.flag_bufs.local(((R - 1) * per,), torch.int32).zero_()
+                torch.cuda.synchronize()
+                dist.barrier(group=group)
+                return
             self.out_bufs = PeerBuffers(M * N * 2, group)
             self.recv_bufs = PeerBuffers((R - 1) * (M // R) * N * 2, group)
-            self.flag_bufs = PeerBuffers((R - 1) * per * 4, group)
             self.flag_bufs.local(((R - 1) * per,), torch.int32).zero_()
             torch.cuda.synchronize()
             dist.barrier(group=group)          # every flag array is zero before first use
             self.out = self.out_bufs.local((M, N), torch.bfloat16)
             self._outs = (ctypes.c_void_p * R)(*self.out_bufs.ptrs)
             self._recvs = (ctypes.c_void_p * R)(*self.recv_bufs.ptrs)
-            self._flags = (ctypes.c_void_p * R)(*self.flag_bufs.ptrs)
-            self.epoch = 0
             return
         if reduce == "nvls":
             # one symmetric bf16 buffer: the GEMM writes this rank's partial
@@ -410,11 +419,20 @@ class RowParallelFP8:
                                             self.chunks, self.comm_sms, self.group)
         if self.reduce == "nvls":
             return self._nvls(a_codes_shard, sa, w_codes_shard, sw, Kr, entry_barrier)
-        if self.reduce == "fused":
+        if self.reduce in ("fused", "fused_nvls"):
             # the ranks' GEMMs start together (the flag waits are bounded), and
             # every sum is in every output after the exit barrier
             self.barrier()
             self.epoch += 1
+            if self.reduce == "fused_nvls":
+                check(l.kc_gemm_fp8_allreduce_mc(
+                    ctypes.c_void_p(a_codes_shard.data_ptr()), ctypes.c_void_p(sa.data_ptr()),
+                    ctypes.c_void_p(w_codes_shard.data_ptr()), ctypes.c_void_p(sw.data_ptr()),
+                    ctypes.c_void_p(self.out.data_ptr()), ctypes.c_void_p(self.symm.multicast_ptr),
+                    self._flags, self.world, self.rank, self.epoch, self.M, self.N, Kr,
+                    self.barrier.timeout_ns, _stream()))
+                self.barrier()
+                return self.out
             check(l.kc_gemm_fp8_allreduce(
                 ctypes.c_void_p(a_codes_shard.data_ptr()), ctypes.c_void_p(sa.data_ptr()),
                 ctypes.c_void_p(w_codes_shard.data_ptr()), ctypes.c_void_p(sw.data_ptr()),
@@ -477,6 +495,10 @@ class RowParallelFP8:
         self.barrier.close()
         if self.reduce == "nvls":
             self.symm.close()
+            return
+        if self.reduce == "fused_nvls":
+            self.symm.close()
+            self.flag_bufs.close()
             return
         if self.reduce == "fused":
             self.out_bufs.close()

@@ -11,7 +11,7 @@ kc_allreduce_bf16_peer -- against the single-GPU FP8 GEMM, normwise <= 1e-2
 (bf16 partials are rounded before the sum); the peer sum is identical on
 every rank; so are the sum fused into the GEMM epilogue
 (kc_gemm_fp8_allreduce: partial tiles to their row owner, the owner's bf16
-sum to every rank) and the in-switch sum (RowParallelFP8 reduce="nvls":
+sum to every rank) and the in-switch sums (RowParallelFP8 reduce="nvls" and "fused_nvls":
 multimem.ld_reduce / multimem.st through NVLink SHARP, where the platform has
 multicast).  MLP block (tp.MLPBlockW4A16, the reference's col-parallel ->
 GELU -> row-parallel chain): the sharded block against the two unsharded
@@ -118,21 +118,24 @@ def _rank_main(rank, world, port, out_dir):
         fused_same = float(all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16))
                                for g in gathered))
         rf.close()
-        # the in-switch sum (NVLink SHARP multicast), two row blocks, twice in a
-        # row (the second call reuses the symmetric buffer behind the barriers)
-        try:
-            rn = tp.RowParallelFP8(M2, N2, reduce="nvls", chunks=2)
-        except RuntimeError:
-            nvls_err, nvls_same = -1.0, -1.0           # no multicast on this platform
-        else:
+        # the in-switch sum (NVLink SHARP multicast): after the GEMM in two row
+        # blocks, and inside the GEMM's epilogue; each twice in a row (the
+        # second call reuses the symmetric buffer behind the barriers)
+        nvls_err, nvls_same = -1.0, -1.0               # stay -1 without multicast
+        for mode in ("nvls", "fused_nvls"):
+            try:
+                rn = tp.RowParallelFP8(M2, N2, reduce=mode, chunks=2)
+            except RuntimeError:
+                continue
             rn(qa_s, sa, qw_s, sw)
             y4 = rn(qa_s, sa, qw_s, sw, entry_barrier=True).clone()
             torch.cuda.synchronize()
-            nvls_err = float((y4.float() - ref).abs().max() / ref.abs().max())
+            nvls_err = max(nvls_err, float((y4.float() - ref).abs().max() / ref.abs().max()))
             gathered = [torch.empty_like(y4) for _ in range(world)]
             dist.all_gather(gathered, y4)
-            nvls_same = float(all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16))
-                                  for g in gathered))
+            same = float(all(torch.equal(gathered[0].view(torch.int16), g.view(torch.int16))
+                             for g in gathered))
+            nvls_same = same if nvls_same < 0 else min(nvls_same, same)
             rn.close()
 
         # MLP block: W1 [I, H] by rows, W2 [H, I] by the same columns, one all-reduce

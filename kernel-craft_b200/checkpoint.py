@@ -33,7 +33,7 @@ producer of x).
 """
 from __future__ import annotations
 
-from typing import NamedTuple, Optional, Tuple
+from typing import Dict, NamedTuple, Optional, Tuple
 
 import numpy as np
 
@@ -177,3 +177,73 @@ def to_reference_abi(w: W4A16Weights, group_size: int = 128) -> Tuple[np.ndarray
                                  "row r+1's first; these zero points differ there")
             zeros[N * stride] = zp[N - 1, G - 1]
     return packed, w.scales.astype(np.float32), zeros
+
+
+# ---------------------------------------------------------------------------
+# On-disk form of converted weights
+# ---------------------------------------------------------------------------
+# One .npz archive per model: for every layer name the arrays "<name>.packed"
+# (u8 [N, K/2]), "<name>.scales" (fp16 [N, K/gs]) and, where present,
+# "<name>.perm" (int64 [K]) and "<name>.zeros" (u8 [N, K/gs]); plus
+# "__kc_w4a16__" = [format version, group size].  The arrays are stored
+# exactly as the kernels read them, so loading is a file read and a copy to
+# the device -- no conversion at start-up.
+
+FORMAT_VERSION = 1
+_HEADER = "__kc_w4a16__"
+
+
+def _check_layer(name: str, w: W4A16Weights, group_size: int) -> None:
+    p, s = np.asarray(w.packed), np.asarray(w.scales)
+    if p.dtype != np.uint8 or p.ndim != 2:
+        raise ValueError(f"{name}: packed must be u8 [N, K/2], got {p.dtype} {p.shape}")
+    N, K = p.shape[0], 2 * p.shape[1]
+    if K % group_size:
+        raise ValueError(f"{name}: K={K} is not a multiple of the group size {group_size}")
+    if s.dtype != np.float16 or s.shape != (N, K // group_size):
+        raise ValueError(f"{name}: scales must be fp16 [{N}, {K // group_size}], got {s.dtype} {s.shape}")
+    if w.perm is not None:
+        perm = np.asarray(w.perm)
+        if perm.shape != (K,) or not np.array_equal(np.sort(perm), np.arange(K)):
+            raise ValueError(f"{name}: perm must be a permutation of {K} input channels")
+    if w.zeros is not None:
+        z = np.asarray(w.zeros)
+        if z.dtype != np.uint8 or z.shape != (N, K // group_size) or np.any(z > 15):
+            raise ValueError(f"{name}: zeros must be u8 [{N}, {K // group_size}] in 0..15")
+
+
+def save(path, layers: Dict[str, W4A16Weights], group_size: int = 128) -> None:
+    """Write converted layers (name -> W4A16Weights) to one .npz archive."""
+    arrays = {_HEADER: np.array([FORMAT_VERSION, group_size], np.int64)}
+    for name, w in layers.items():
+        if "." in name or name == _HEADER:
+            raise ValueError(f"layer name {name!r} must not contain '.'")
+        _check_layer(name, w, group_size)
+        arrays[f"{name}.packed"] = np.ascontiguousarray(w.packed)
+        arrays[f"{name}.scales"] = np.ascontiguousarray(w.scales)
+        if w.perm is not None:
+            arrays[f"{name}.perm"] = np.asarray(w.perm, np.int64)
+        if w.zeros is not None:
+            arrays[f"{name}.zeros"] = np.ascontiguousarray(w.zeros)
+    np.savez(path, **arrays)
+
+
+def load(path) -> Tuple[Dict[str, W4A16Weights], int]:
+    """Read an archive written by save(): (name -> W4A16Weights, group size).
+    Every layer is checked against the layout the kernels expect."""
+    with np.load(path, allow_pickle=False) as f:
+        if _HEADER not in f.files:
+            raise ValueError(f"{path}: not a W4A16 weight archive (no {_HEADER} entry)")
+        version, group_size = (int(v) for v in f[_HEADER])
+        if version != FORMAT_VERSION:
+            raise ValueError(f"{path}: format version {version}, this library reads {FORMAT_VERSION}")
+        names = sorted({k.split(".")[0] for k in f.files if k != _HEADER})
+        layers = {}
+        for name in names:
+            get = lambda part: f[f"{name}.{part}"] if f"{name}.{part}" in f.files else None
+            if get("packed") is None or get("scales") is None:
+                raise ValueError(f"{path}: layer {name!r} lacks packed weights or scales")
+            w = W4A16Weights(get("packed"), get("scales"), get("perm"), get("zeros"))
+            _check_layer(name, w, group_size)
+            layers[name] = w
+    return layers, group_size

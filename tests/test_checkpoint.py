@@ -184,3 +184,45 @@ def test_reference_abi_form(packers, K, gs):
     packed, scales32, zeros = C.to_reference_abi(w, gs)
     got = O.dequantize_int4(packed, scales32, zeros, N, K, gs)
     np.testing.assert_array_equal(got, _dequant_checkpoint(u, s, z, np.arange(K) // gs))
+
+
+def test_archive_round_trip(packers, tmp_path):
+    """checkpoint.save / load: converted layers (symmetric, asymmetric, act
+    order) come back bit for bit, with the group size."""
+    K, N, gs = 512, 24, 128
+    u, s, z = _inputs(K, N, gs, seed=41, zero=None)
+    g_idx = np.random.default_rng(42).permutation(np.arange(K) // gs)
+    layers = {
+        "qkv": C.from_gptq(packers[0](u), packers[1](np.full_like(z, 8)), s, group_size=gs,
+                           checkpoint_format="gptq_v2"),
+        "o": C.from_awq(packers[2](u), packers[2](z), s, group_size=gs),
+        "down": C.from_gptq(packers[0](u), packers[1](z), s, g_idx=g_idx, group_size=gs,
+                            checkpoint_format="gptq_v2"),
+    }
+    path = tmp_path / "model.npz"
+    C.save(path, layers, gs)
+    back, g = C.load(path)
+    assert g == gs and sorted(back) == sorted(layers)
+    for name, w in layers.items():
+        b = back[name]
+        np.testing.assert_array_equal(b.packed, w.packed)
+        np.testing.assert_array_equal(b.scales.view(np.uint16), w.scales.view(np.uint16))
+        for part in ("perm", "zeros"):
+            x, y = getattr(w, part), getattr(b, part)
+            assert (x is None) == (y is None)
+            if x is not None:
+                np.testing.assert_array_equal(x, y)
+
+
+def test_archive_rejects_bad_layers(tmp_path):
+    K, N, gs = 256, 8, 128
+    good = C.W4A16Weights(np.zeros((N, K // 2), np.uint8), np.ones((N, K // gs), np.float16), None)
+    with pytest.raises(ValueError, match="scales"):
+        C.save(tmp_path / "a.npz", {"l": good._replace(scales=np.ones((N, 3), np.float16))}, gs)
+    with pytest.raises(ValueError, match="zeros"):
+        C.save(tmp_path / "b.npz", {"l": good._replace(zeros=np.full((N, K // gs), 16, np.uint8))}, gs)
+    with pytest.raises(ValueError, match="'.'"):
+        C.save(tmp_path / "c.npz", {"a.b": good}, gs)
+    np.savez(tmp_path / "d.npz", x=np.zeros(3))
+    with pytest.raises(ValueError, match="not a W4A16 weight archive"):
+        C.load(tmp_path / "d.npz")

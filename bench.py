@@ -254,10 +254,11 @@ class GemvW4A16(Workload):
     kernel = "gemv_w4a16"
     profile = "gemv_w4a16_7b_decode_m1"
 
-    def __init__(self, torch, l, dev, s_ptr, rank, world=1, layers=LAYERS):
+    def __init__(self, torch, l, dev, s_ptr, rank, world=1, layers=LAYERS, weights="tiled"):
         super().__init__(torch, l, dev, s_ptr, rank, world)
         import kc_lib
         self.kc_lib = kc_lib
+        self.weights = weights
         self.n_layers = layers
         self.launches_per_step = layers
         self.layers = []
@@ -281,19 +282,39 @@ class GemvW4A16(Workload):
                 xo += K
                 yo += N
                 probs.append((packed, scales, x, y, N, K))
+            tiled = None
+            if self.weights == "tiled":
+                # the library's tile-ordered layout, converted once like a
+                # checkpoint at load time; the packed copy is dropped
+                tiled = []
+                for i, (p, sc, x, y, N, K) in enumerate(probs):
+                    t = torch.empty(((N + 15) // 16 * 16) * (K // 2), dtype=torch.uint8, device=dev)
+                    kc_lib.check(l.kc_w4a16_tile_weights(p.data_ptr(), t.data_ptr(), N, K, s_ptr))
+                    tiled.append(t)
+                torch.cuda.synchronize()
+                probs = [(None, sc, x, y, N, K) for (_, sc, x, y, N, K) in probs]
             arr = (kc_lib.W4A16Problem * 4)(*[
-                kc_lib.W4A16Problem(p.data_ptr(), s.data_ptr(), x.data_ptr(), y.data_ptr(), N, K)
+                kc_lib.W4A16Problem(p.data_ptr() if p is not None else None, s.data_ptr(), x.data_ptr(),
+                                    y.data_ptr(), N, K)
                 for p, s, x, y, N, K in probs])
-            self.layers.append((probs, arr))
+            tarr = (ctypes.c_void_p * 4)(*[t.data_ptr() for t in tiled]) if tiled else None
+            self.layers.append((probs, arr, tiled, tarr))
 
     use_graph = True      # replay the step's launches as one CUDA graph (--no-graph: eager)
+
+    def _grouped(self, layer, st):
+        _, arr, _, tarr = layer
+        if tarr is not None:
+            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped_tiled(arr, tarr, None, 4, 1, GROUP, st))
+        else:
+            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, st))
 
     def _launch_all(self):
         # launched on the current stream: the capture stream inside the graph
         # capture, the bench's stream otherwise
         st = ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
-        for _, arr in self.layers:
-            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, st))
+        for layer in self.layers:
+            self._grouped(layer, st)
 
     def _capture(self):
         """The step's 32 grouped launches as one CUDA graph (captured after one
@@ -330,6 +351,8 @@ class GemvW4A16(Workload):
     def config(self):
         return {"workload": self.workload_id, "layers": self.n_layers,
                 "shapes_KN": [[K, N] for _, K, N in SHAPES], "M": 1, "group_size": GROUP,
+                "weights": ("packed [N, K/2] (the reference layout)" if self.weights == "packed" else
+                            "tile-ordered (kc_w4a16_tile_weights, converted once at load)"),
                 "bytes_per_step": self.work_per_step(),
                 "launch": "one grouped launch per layer" + (
                     ", the step's launches replayed as one CUDA graph" if self.use_graph else
@@ -359,13 +382,13 @@ class GemvW4A16(Workload):
         st = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)  # noqa: E731
         self.part_graphs = []
         for _, _, layers in self.parts:
-            for _, arr in layers:    # one eager pass sets the kernel attributes
-                self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, st()))
+            for layer in layers:    # one eager pass sets the kernel attributes
+                self._grouped(layer, st())
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, capture_error_mode="thread_local"):
-                for _, arr in layers:
-                    self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, st()))
+                for layer in layers:
+                    self._grouped(layer, st())
             self.part_graphs.append(g)
         torch.cuda.synchronize()
         return (self.h_x.numel() * self.h_x.element_size(),
@@ -1112,7 +1135,7 @@ def run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, lo
     JSON line from rank 0.  Returns the exit status (3: the gate failed)."""
     W = WORKLOADS[name]
     if W is GemvW4A16:
-        wl = W(torch, l, dev, s_ptr, rank, world, layers=args.layers)
+        wl = W(torch, l, dev, s_ptr, rank, world, layers=args.layers, weights=args.gemv_weights)
         wl.use_graph = not args.no_graph
     else:
         wl = W(torch, l, dev, s_ptr, rank, world)
@@ -1436,6 +1459,9 @@ def main(argv=None) -> int:
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e pass")
     ap.add_argument("--no-graph", action="store_true",
                     help="gemv: launch the step eagerly instead of replaying it as a CUDA graph")
+    ap.add_argument("--gemv-weights", choices=["packed", "tiled"], default="tiled",
+                    help="gemv: weights in the reference's packed [N, K/2] layout or the library's "
+                         "tile-ordered layout (kc_w4a16_tile_weights, converted once at load)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="gemv: decoder layers per step (default 32; fewer only for profiling)")
     ap.add_argument("--heat-s", type=float, default=1.5,

@@ -233,6 +233,22 @@ KC_API int kc_gemv_w4a16_zp(const uint8_t* packed, const uint16_t* scales_f16, c
 KC_API int kc_gemv_w4a16_grouped_zp(const kc_w4a16_problem* problems, const uint8_t* const* zeros,
                                     int count, int M, int group_size, cudaStream_t stream);
 
+/* Tile-ordered weights (no reference counterpart): the same packed bytes
+ * rearranged so that every 16-row x 128-k chunk (1 KB) is contiguous,
+ * tiled[ceil(N/16)][K/128][16 rows][64 bytes], rows past N zero.  The GEMV
+ * then fetches a stage of up to four chunks with one bulk copy.
+ * kc_w4a16_tile_weights converts packed u8[N, K/2] (K % 128 == 0, 16-byte
+ * aligned) into a buffer of ceil(N/16) * 16 * K/2 bytes, once at load time. */
+KC_API int kc_w4a16_tile_weights(const uint8_t* packed, uint8_t* tiled, int N, int K, cudaStream_t stream);
+/* The grouped GEMV (and its zero-point form, zeros may be NULL) reading
+ * tiled[i] instead of problems[i].packed, which may then be NULL.  Results are
+ * bit-identical to kc_gemv_w4a16_grouped[_zp].  Only the tensor-core paths
+ * read the tiled form: K % 128 == 0, group_size = 128 * 2^m, 16-byte aligned
+ * buffers, zero points at batch 1 only; other shapes are refused. */
+KC_API int kc_gemv_w4a16_grouped_tiled(const kc_w4a16_problem* problems, const uint8_t* const* tiled,
+                                       const uint8_t* const* zeros, int count, int M, int group_size,
+                                       cudaStream_t stream);
+
 /* FP8 E4M3 per-token quantization (fp8_quant.cu:89-131 semantics, bit-exact):
  * scales[r] = amax_r > 0 ? amax_r/448 : 1; q = e4m3_satfinite(clamp(x/scale)). */
 KC_API int kc_quantize_fp8_per_token(const float* in, int8_t* out, float* scales,

@@ -179,6 +179,21 @@ def to_reference_abi(w: W4A16Weights, group_size: int = 128) -> Tuple[np.ndarray
     return packed, w.scales.astype(np.float32), zeros
 
 
+def tile_w4(packed: np.ndarray) -> np.ndarray:
+    """packed u8 [N, K/2] -> the tile-ordered layout the W4A16 GEMV streams
+    fastest (kc_w4a16_tile_weights does the same on the GPU): every 16-row x
+    128-k chunk contiguous, [ceil(N/16)][K/128][16 rows][64 bytes], rows past
+    N zero.  K must be a multiple of 128."""
+    p = np.asarray(packed)
+    N, half = p.shape
+    if p.dtype != np.uint8 or half % 64:
+        raise ValueError("packed must be u8 [N, K/2] with K a multiple of 128")
+    Np = (N + 15) // 16 * 16
+    pad = np.zeros((Np, half), np.uint8)
+    pad[:N] = p
+    return pad.reshape(Np // 16, 16, half // 64, 64).transpose(0, 2, 1, 3).reshape(-1).copy()
+
+
 # ---------------------------------------------------------------------------
 # On-disk form of converted weights
 # ---------------------------------------------------------------------------

@@ -48,6 +48,10 @@ namespace {
 
 struct Prob {
     const uint8_t* packed;
+    // or the same weights in tile order: [ceil(N/16)][K/128][16 rows][64 B],
+    // every 16-row x 128-k chunk contiguous (kc_w4a16_tile_weights); a ring
+    // stage is then one bulk copy instead of one 2-D box per chunk
+    const uint8_t* tiled;
     const __half* scales;
     const uint8_t* zeros;  // per-group zero points u8[N, K/gs] (0..15); null: 8 (symmetric GPTQ)
     const __nv_bfloat16* x;
@@ -205,6 +209,20 @@ __device__ __forceinline__ void issue_quad(const Params& P, Cursor& cu, uint32_t
     if (cu.tile >= P.total_tiles) return;
     const int row0 = (cu.tile - P.p[cu.pi].tile_begin) * 16;
     const int n = min(kQuad, cu.cend - cu.c);
+    if (const uint8_t* tiled = P.p[cu.pi].tiled) {
+        // the quad's chunks are consecutive k-chunks of one tile: contiguous
+        const uint8_t* src = tiled + ((size_t)(row0 >> 4) * (P.p[cu.pi].K >> 7) + cu.c) * kChunkBytes;
+        asm volatile(
+            "{\n\t.reg .pred l;\n\t"
+            "setp.ne.b32 l, %0, 0;\n\t"
+            "@l mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n\t"
+            "@l cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%3], [%4], %2, [%1];\n\t}"
+            ::"r"((int)leader), "r"(bar), "r"((uint32_t)n * kChunkBytes), "r"(dst), "l"(src)
+            : "memory");
+        cu.c += n;
+        cursor_settle(P, cu, warp);
+        return;
+    }
     const CUtensorMap* map = &P.wmap[cu.pi];
     const int x0 = cu.c * 64;
     asm volatile(
@@ -1108,7 +1126,7 @@ int launch(Params& P, cudaStream_t stream) {
         // last tile's block must stay a multiple of 16 bytes.
         const long row_bytes = 2L * (p.K / P.gs);
         const int tail = p.N % 16;
-        fast = (p.K % 128 == 0) && kc::aligned(p.packed, 16) && kc::aligned(p.x, 16) &&
+        fast = (p.K % 128 == 0) && kc::aligned(p.tiled ? p.tiled : p.packed, 16) && kc::aligned(p.x, 16) &&
                kc::aligned(p.scales, 16) && 16 * row_bytes <= 2L * kScaleHalves &&
                (16 * row_bytes) % 16 == 0 && (tail == 0 || (tail * row_bytes) % 16 == 0);
         single_group = single_group && (p.K == P.gs);
@@ -1123,6 +1141,10 @@ int launch(Params& P, cudaStream_t stream) {
     // zero points: the batch-1 integer path (below) takes them; the bf16
     // paths do not, so other batch sizes run on the CUDA-core kernel
     if (!fast || gshift < 0 || (any_zeros && P.M != 1)) {
+        for (int i = 0; i < P.count; ++i)
+            KC_REQUIRE(P.p[i].packed != nullptr, KC_ERR_INVALID_ARG,
+                       "tile-ordered weights run on the tensor-core paths only (K %% 128 == 0, "
+                       "group size 128 x 2^m, 16-byte aligned, zero points only at batch 1)");
         long rows = 0;
         for (int i = 0; i < P.count; ++i) rows += P.p[i].N;
         const long blocks = (rows + 7) / 8;
@@ -1132,6 +1154,7 @@ int launch(Params& P, cudaStream_t stream) {
     }
     for (int i = 0; i < P.count; ++i) {
         const Prob& p = P.p[i];
+        if (p.tiled) continue;   // bulk copies, no tensor map
         const int st = kc::encode_2d(&P.wmap[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, p.packed,
                                      (uint64_t)(p.K / 2), (uint64_t)p.N, (uint64_t)(p.K / 2), 64, 16,
                                      CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -1157,6 +1180,9 @@ int launch(Params& P, cudaStream_t stream) {
                          : launch_i8<false>(P, (size_t)chunks * kI8ChunkBytes, stream);
     }
     if (any_zeros) {   // batch 1 whose activations do not fit the staging: CUDA cores
+        for (int i = 0; i < P.count; ++i)
+            KC_REQUIRE(P.p[i].packed != nullptr, KC_ERR_INVALID_ARG,
+                       "tile-ordered weights with zero points need the batch-1 staged path");
         long rows = 0;
         for (int i = 0; i < P.count; ++i) rows += P.p[i].N;
         const long blocks = (rows + 7) / 8;
@@ -1174,6 +1200,23 @@ int launch(Params& P, cudaStream_t stream) {
     return stage ? launch_tc<2, true>(P, stage_bytes, stream) : launch_tc<2, false>(P, 0, stream);
 }
 
+// packed [N, K/2] -> tile order [ceil(N/16)][K/128][16][64 B], rows past N zero;
+// one 16-byte piece per thread and step
+__global__ void tile_weights_kernel(const uint8_t* __restrict__ packed, uint8_t* __restrict__ tiled, int N,
+                                    int K, long pieces) {
+    const int chunks = K / 128;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < pieces; i += (long)gridDim.x * blockDim.x) {
+        const int b16 = (int)(i & 3), r = (int)((i >> 2) & 15);
+        const long tc = i >> 6;                       // tile * chunks + chunk
+        const int c = (int)(tc % chunks);
+        const long t = tc / chunks;
+        const long row = t * 16 + r;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (row < N) v = *reinterpret_cast<const uint4*>(packed + row * (K / 2) + (long)c * 64 + b16 * 16);
+        *reinterpret_cast<uint4*>(tiled + i * 16) = v;
+    }
+}
+
 }  // namespace
 
 KC_DEFINE_STATUS_READER(gemv)
@@ -1182,7 +1225,7 @@ extern "C" {
 
 namespace {
 int gemv_grouped(const kc_w4a16_problem* problems, const uint8_t* const* zeros, int count, int M,
-                 int gs, cudaStream_t stream) {
+                 int gs, cudaStream_t stream, const uint8_t* const* tiled = nullptr) {
     KC_REQUIRE(problems != nullptr, KC_ERR_INVALID_ARG, "null problem list");
     KC_REQUIRE(count >= 1 && count <= KC_W4A16_MAX_PROBLEMS, KC_ERR_INVALID_ARG,
                "count=%d outside 1..%d", count, KC_W4A16_MAX_PROBLEMS);
@@ -1201,11 +1244,12 @@ int gemv_grouped(const kc_w4a16_problem* problems, const uint8_t* const* zeros, 
     long tiles = 0;
     for (int i = 0; i < count; ++i) {
         const kc_w4a16_problem& q = problems[order[i]];
-        KC_REQUIRE(q.packed && q.scales_f16 && q.x_bf16 && q.y, KC_ERR_INVALID_ARG,
-                   "problem %d has a null pointer", order[i]);
+        KC_REQUIRE((q.packed || (tiled && tiled[order[i]])) && q.scales_f16 && q.x_bf16 && q.y,
+                   KC_ERR_INVALID_ARG, "problem %d has a null pointer", order[i]);
         KC_REQUIRE(q.N >= 0 && q.K > 0 && q.K % 2 == 0 && q.K % gs == 0, KC_ERR_INVALID_ARG,
                    "problem %d: bad shape N=%d K=%d for group_size=%d", order[i], q.N, q.K, gs);
         P.p[i].packed = q.packed;
+        P.p[i].tiled = tiled ? tiled[order[i]] : nullptr;
         P.p[i].scales = reinterpret_cast<const __half*>(q.scales_f16);
         P.p[i].zeros = zeros ? zeros[order[i]] : nullptr;
         P.p[i].x = reinterpret_cast<const __nv_bfloat16*>(q.x_bf16);
@@ -1230,6 +1274,28 @@ int kc_gemv_w4a16_grouped_zp(const kc_w4a16_problem* problems, const uint8_t* co
                              int count, int M, int gs, cudaStream_t stream) {
     KC_REQUIRE(zeros != nullptr, KC_ERR_INVALID_ARG, "null zero-point list");
     return gemv_grouped(problems, zeros, count, M, gs, stream);
+}
+
+int kc_gemv_w4a16_grouped_tiled(const kc_w4a16_problem* problems, const uint8_t* const* tiled,
+                                const uint8_t* const* zeros, int count, int M, int gs,
+                                cudaStream_t stream) {
+    KC_REQUIRE(tiled != nullptr, KC_ERR_INVALID_ARG, "null tile-ordered weight list");
+    for (int i = 0; i < count && i < KC_W4A16_MAX_PROBLEMS; ++i)
+        KC_REQUIRE(tiled[i] != nullptr, KC_ERR_INVALID_ARG, "problem %d: null tile-ordered weights", i);
+    return gemv_grouped(problems, zeros, count, M, gs, stream, tiled);
+}
+
+int kc_w4a16_tile_weights(const uint8_t* packed, uint8_t* tiled, int N, int K, cudaStream_t stream) {
+    KC_REQUIRE(packed && tiled, KC_ERR_INVALID_ARG, "null pointer argument");
+    KC_REQUIRE(N >= 0 && K > 0 && K % 128 == 0, KC_ERR_INVALID_ARG,
+               "N=%d, K=%d: K must be a positive multiple of 128", N, K);
+    KC_REQUIRE(kc::aligned(packed, 16) && kc::aligned(tiled, 16), KC_ERR_ALIGNMENT,
+               "buffers must be 16-byte aligned");
+    if (N == 0) return KC_OK;
+    const long pieces = (long)((N + 15) / 16) * (K / 128) * 64;   // 16-byte pieces
+    tile_weights_kernel<<<(unsigned)std::min<long>((pieces + 255) / 256, (long)kc::sm_count() * 16), 256, 0,
+                          stream>>>(packed, tiled, N, K, pieces);
+    return kc::check_launch("w4a16_tile_weights");
 }
 
 int kc_gemv_w4a16(const uint8_t* packed, const uint16_t* scales_f16, const uint16_t* x_bf16,

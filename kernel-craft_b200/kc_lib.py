@@ -89,6 +89,8 @@ _PROTOS = [
     ("kc_gemv_w4a16_grouped", ci, [ctypes.POINTER(W4A16Problem), ci, ci, ci, vp]),
     ("kc_gemv_w4a16_zp", ci, [vp, vp, vp, vp, vp, ci, ci, ci, ci, vp]),
     ("kc_gemv_w4a16_grouped_zp", ci, [ctypes.POINTER(W4A16Problem), ctypes.POINTER(vp), ci, ci, ci, vp]),
+    ("kc_w4a16_tile_weights", ci, [vp, vp, ci, ci, vp]),
+    ("kc_gemv_w4a16_grouped_tiled", ci, [ctypes.POINTER(W4A16Problem), ctypes.POINTER(vp), ctypes.POINTER(vp), ci, ci, ci, vp]),
     ("kc_quantize_fp8_per_token", ci, [vp, vp, vp, ci, ci, vp]),
     ("kc_quantize_fp8_per_channel", ci, [vp, vp, vp, ci, ci, vp]),
     ("kc_quantize_fp8_per_tensor", ci, [vp, vp, vp, cl, vp]),

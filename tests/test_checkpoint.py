@@ -226,3 +226,24 @@ def test_archive_rejects_bad_layers(tmp_path):
     np.savez(tmp_path / "d.npz", x=np.zeros(3))
     with pytest.raises(ValueError, match="not a W4A16 weight archive"):
         C.load(tmp_path / "d.npz")
+
+
+def test_tile_w4_layout():
+    """checkpoint.tile_w4: chunk (tile t, k-chunk c) is the 1 KB at
+    (t * K/128 + c) * 1024, its row r the 64 bytes packed[16 t + r, 64 c:64 c + 64],
+    rows past N zero."""
+    rng = np.random.default_rng(3)
+    N, K = 40, 512
+    p = rng.integers(0, 256, (N, K // 2), dtype=np.uint8)
+    t = C.tile_w4(p)
+    C_ = K // 128
+    assert t.shape == (48 * K // 2,)
+    for tile in range(3):
+        for c in range(C_):
+            blk = t[(tile * C_ + c) * 1024:(tile * C_ + c + 1) * 1024].reshape(16, 64)
+            for r in range(16):
+                row = tile * 16 + r
+                want = p[row, 64 * c:64 * c + 64] if row < N else np.zeros(64, np.uint8)
+                np.testing.assert_array_equal(blk[r], want)
+    with pytest.raises(ValueError):
+        C.tile_w4(p[:, :100])

@@ -6,6 +6,8 @@ Bars (written here, from the task's parity rules):
   * GEMV outputs (fp32 accumulation): normwise max|y-ref|/max|ref| <= 1e-3,
     and the reference C++ test's own bound (|err| < 1e-4) on its 16x16 KAT.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -343,3 +345,47 @@ def test_w4a16_batch1_all_zero_row(cuda):
     x = np.zeros((1, K), np.uint16)
     y = _run_w4a16(packed, scales, x, 1, N, K, gs)
     assert np.all(y == 0)
+
+
+@pytest.mark.parametrize("M,zp", [(1, False), (1, True), (4, False), (16, False)])
+def test_w4a16_tiled_layout_matches_packed(cuda, M, zp):
+    """kc_w4a16_tile_weights + kc_gemv_w4a16_grouped_tiled: the tile-ordered
+    weights give bit-identical outputs to the packed layout through the same
+    kernels (the 7B shapes plus a ragged N, with and without zero points),
+    and the conversion itself matches a numpy restatement of the layout."""
+    gs = 128
+    shapes = SEVEN_B + [(1024, 200)]
+    l = kc_lib.lib()
+    probs, tiled, zps, keep = [], [], [], []
+    for i, (K, N) in enumerate(shapes):
+        packed, scales, x = _w4a16_inputs(M, N, K, gs, seed=900 + 10 * M + i)
+        dp, ds, dx = dev(packed), dev(scales), dev(x).view(torch.bfloat16)
+        t = torch.empty(((N + 15) // 16 * 16) * (K // 2), dtype=torch.uint8, device=cuda)
+        kc_lib.check(l.kc_w4a16_tile_weights(ptr(dp), ptr(t), N, K, stream()))
+        z = dev(np.random.default_rng(i).integers(0, 16, (N, K // gs), dtype=np.uint8)) if zp else None
+        y = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+        keep.append((packed, dp, ds, dx, t, z, y, N, K))
+        probs.append(kc_lib.W4A16Problem(dp.data_ptr(), ds.data_ptr(), dx.data_ptr(), y.data_ptr(), N, K))
+        tiled.append(t.data_ptr())
+        zps.append(z.data_ptr() if z is not None else None)
+    n = len(shapes)
+    arr = (kc_lib.W4A16Problem * n)(*probs)
+    zarr = (ctypes.c_void_p * n)(*zps) if zp else None
+    if zp:
+        kc_lib.check(l.kc_gemv_w4a16_grouped_zp(arr, zarr, n, M, gs, stream()))
+    else:
+        kc_lib.check(l.kc_gemv_w4a16_grouped(arr, n, M, gs, stream()))
+    want = [host(k[6]).copy() for k in keep]
+    for k in keep:
+        k[6].fill_(float("nan"))
+    # the tiled call with the packed pointers removed: only the tiled bytes are read
+    arr2 = (kc_lib.W4A16Problem * n)(*[
+        kc_lib.W4A16Problem(None, p.scales_f16, p.x_bf16, p.y, p.N, p.K) for p in probs])
+    kc_lib.check(l.kc_gemv_w4a16_grouped_tiled(arr2, (ctypes.c_void_p * n)(*tiled), zarr, n, M, gs, stream()))
+    for (packed, _, _, _, t, _, y, N, K), w in zip(keep, want):
+        np.testing.assert_array_equal(host(y), w)
+        Np = (N + 15) // 16 * 16
+        ref = np.zeros((Np, K // 2), np.uint8)
+        ref[:N] = packed
+        ref = ref.reshape(Np // 16, 16, K // 128, 64).transpose(0, 2, 1, 3).reshape(-1)
+        np.testing.assert_array_equal(host(t), ref)

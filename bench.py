@@ -6,14 +6,19 @@
 
 With no --workload (``all``) one JSON line is printed per workload, in the
 order gemv_int4, quant_fp8, gemm_w4a16, gemm_fp8, and last the headline
-decode-GEMV line ("W4A16 GEMV HBM GB/s"):
+decode-GEMV line ("W4A16 GEMV HBM GB/s"); the headline is measured first
+(after its own heat phase, on a GPU the GEMMs have not heated) and printed
+last:
 
   gemv        the Llama-style 7B decode linear set at batch M = 1 -- per
               layer the K->N projections 4096->12288 (QKV), 4096->4096 (O),
               4096->22016 (gate+up) and 11008->4096 (down); GPTQ INT4 weights
               (uniform nibbles, implicit zero-point 8, group 128, fp16 scales
               U[0.002, 0.02]); bf16 activations N(0,1); fp32 accumulation and
-              output.  One step = one decode token through a 32-layer stack:
+              output; the weights in the library's tile-ordered layout
+              (kc_w4a16_tile_weights, converted once at load; --gemv-weights
+              packed streams the reference's [N, K/2] layout instead, the
+              same bytes).  One step = one decode token through a 32-layer stack:
               32 launches (one grouped launch of a layer's four projections
               each), 3.35 GB of distinct weights per step, so no step reads
               weights from L2 (126 MB).  value = algorithmic bytes per step /
@@ -37,7 +42,8 @@ At N > 1 the sharded GEMMs first pass a correctness gate: the sharded result
 on a small problem is compared with the single-GPU kernel's on the same
 inputs (bit-equal for the column-parallel GEMM, normwise <= 1e-2 for the
 row-parallel one, whose bf16 partials are rounded before the sum); a
-mismatch ends the run with exit code 3 before anything is timed.
+mismatch prints an error line for that workload, which is not timed, and
+the run ends with exit code 3 after the other workloads.
 
 The reference arm (--impl reference) times the reference path's CPU
 restatement (oracle/, "kind": "port" -- the reference ships no CPU
@@ -1062,6 +1068,8 @@ class MlpW4A16(Workload):
 WORKLOADS = {w.name: w for w in (GemvW4A16, GemmW4A16, GemmFP8, QuantFP8, GemvInt4, MlpW4A16)}
 # the default run: one line each, the headline decode GEMV last
 DEFAULT_SET = ("gemv_int4", "quant_fp8", "gemm_w4a16", "gemm_fp8", "gemv")
+# the headline (gemv) is measured first -- in its own heat phase, not on a GPU
+# the GEMMs before it have heated -- and its line is printed last
 
 
 def _selected(args) -> list:
@@ -1130,7 +1138,7 @@ def _max_over_ranks(torch, dist, world, dev, vals):
     return [float(v) for v in t.tolist()]
 
 
-def run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, local) -> int:
+def run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, local, held=None) -> int:
     """One workload: gate (N > 1), warm-up, heat, K timed steps, e2e, one
     JSON line from rank 0.  Returns the exit status (3: the gate failed)."""
     W = WORKLOADS[name]
@@ -1286,7 +1294,10 @@ def run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, lo
             "gpu_launches": wl.launches_per_step * args.steps,
             "clocks": clocks,
         }
-        print(json.dumps(line), flush=True)
+        if held is not None:
+            held.append(json.dumps(line))
+        else:
+            print(json.dumps(line), flush=True)
     wl.close()
     del wl
     torch.cuda.synchronize()
@@ -1503,8 +1514,16 @@ def main(argv=None) -> int:
     # the run goes on to the next workload, so the headline still prints; the
     # exit status stays non-zero
     rc = 0
-    for name in _selected(args):
+    names = _selected(args)
+    held = []
+    if len(names) > 1 and names[-1] == "gemv":
+        names = ["gemv"] + names[:-1]
+        rc = run_workload("gemv", args, torch, dist, l, dev, stream, s_ptr, world, rank, local, held) or rc
+        names = names[1:]
+    for name in names:
         rc = run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, local) or rc
+    for line in held:
+        print(line, flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

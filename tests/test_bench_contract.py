@@ -13,8 +13,9 @@ ROOT = Path(__file__).resolve().parent.parent
 
 @pytest.mark.parametrize("workload", ["gemv", "gemv_int4"])
 def test_reference_arm_line(workload):
+    # the contract, not the speed: one decode layer instead of the full 32
     out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--workload",
-                          workload, "--steps", "1", "--warmup", "3"],
+                          workload, "--steps", "1", "--warmup", "3", "--layers", "1"],
                          capture_output=True, text=True, timeout=600, cwd=ROOT,
                          env={**os.environ, "RANK": "0"})
     assert out.returncode == 0, out.stderr[-2000:]

@@ -13,6 +13,8 @@
 #   tests/test_tensor_parallel.cpp  launch_ring_allreduce, launch_allgather,
 #                                   launch_col/row_parallel_linear, nccl_* (-DHAVE_NCCL)
 #   benchmarks/benchmark_quant.cpp  the four quantization launchers
+#   benchmarks/benchmark_tensor_parallel.cpp  launch_ring_allreduce, launch_allgather,
+#                                   launch_col/row_parallel_linear, nccl_* (-DHAVE_NCCL)
 #   src/python/pybind_transformer.cpp -> kernel_craft_transformer<ext>
 #
 # Each links -lkernels from kernel-craft_b200/lib with an $ORIGIN-relative
@@ -48,6 +50,8 @@ LINK=(-L "$LIBDIR" -lkernels -L "$CUDA_HOME/lib64" -lcudart "$RPATH")
 "$CXX" "${COMMON[@]}" -DHAVE_NCCL "$REF/tests/test_tensor_parallel.cpp" -o "$OUT/test_tensor_parallel" \
   "${LINK[@]}" -lnccl
 "$CXX" "${COMMON[@]}" "$REF/benchmarks/benchmark_quant.cpp" -o "$OUT/benchmark_quant" "${LINK[@]}"
+"$CXX" "${COMMON[@]}" -DHAVE_NCCL "$REF/benchmarks/benchmark_tensor_parallel.cpp" \
+  -o "$OUT/benchmark_tensor_parallel" "${LINK[@]}" -lnccl
 
 PYBIND_INC="$("$PY" -c 'import pybind11; print(pybind11.get_include())')"
 PY_INC="$("$PY" -c 'import sysconfig; print(sysconfig.get_paths()["include"])')"

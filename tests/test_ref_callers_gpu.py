@@ -5,7 +5,8 @@ this library (oracle/build_ref_callers.sh), run on the B200.
   tests/test_tensor_parallel.cpp (with -DHAVE_NCCL) -- the reference's C++
   unit tests for the launchers this library replaces: exit status 0 and no
   "[FAIL]" line, with their own tolerances;
-* benchmarks/benchmark_quant.cpp -- runs to completion;
+* benchmarks/benchmark_quant.cpp and benchmarks/benchmark_tensor_parallel.cpp
+  -- run to completion;
 * src/python/pybind_transformer.cpp (module kernel_craft_transformer) --
   imports against libkernels.so, and its quantization and tensor-parallel
   functions agree with the oracle: dequantized INT4 weights, FP8 codes and
@@ -55,6 +56,18 @@ def test_reference_quant_benchmark_runs(cuda):
     print(out.stdout[-4000:])
     assert out.returncode == 0, (out.stdout + out.stderr)[-4000:]
     assert "GB/s" in out.stdout
+
+
+def test_reference_tensor_parallel_benchmark_runs(cuda, tmp_path):
+    """benchmarks/benchmark_tensor_parallel.cpp: the simulated collectives and
+    the parallel linears at its own sizes (it appends a report file in its
+    working directory, here a temporary one); its same-device NCCL case
+    reports that NCCL refused and skips, as the reference handles it."""
+    out = subprocess.run([str(_binary("benchmark_tensor_parallel"))], capture_output=True, text=True,
+                         timeout=300, cwd=tmp_path)
+    print(out.stdout[-4000:])
+    assert out.returncode == 0, (out.stdout + out.stderr)[-4000:]
+    assert "Benchmark complete" in out.stdout and "GB/s" in out.stdout
 
 
 @pytest.fixture(scope="module")

@@ -660,8 +660,9 @@ class GemmFP8(Workload):
         if world > 1:
             import tp
             # measured (whole-GEMM TFLOP/s; one GPU 2175): the sum fused into
-            # the GEMM epilogue 2726 on 2 B200s and 2257 on 4; NCCL after the
-            # GEMM 2018 / 2023; the in-switch sum per row block 1771 / 1951
+            # the GEMM epilogue 2726 / 2257 / 1980 on 2 / 4 / 8 B200s; NCCL
+            # after the GEMM 2018 / 2023 / 1602; the in-switch sum per row
+            # block 1771 / 1951 / 1527
             reduce = os.environ.get("KC_TP_REDUCE", "fused")
             kw = dict(chunks=int(os.environ.get("KC_TP_CHUNKS", "4")),
                       comm_sms=int(os.environ.get("KC_TP_COMM_SMS", "16")))

@@ -73,6 +73,15 @@ def test_built_for_sm100a_only():
     lambda l: l.kc_sgemm_nt(1, 1, 1, -1, 4, 4, None),
     lambda l: l.kc_dequantize_w4_bf16(1, 1, 1, 4, 6, 4, None),              # gs !| K
     lambda l: l.kc_nccl_comm_init_rank(None, 2, None, 0),
+    # the fused collectives and the tile-ordered layout
+    lambda l: l.kc_gemm_fp8_allreduce(1, 1, 1, 1, None, None, None, 2, 0, 1, 512, 512, 64, 0, None),
+    lambda l: l.kc_gemm_fp8_allreduce_mc(1, 1, 1, 1, None, None, None, 2, 0, 1, 512, 512, 64, 0, None),
+    lambda l: l.kc_allreduce_bf16_nvls(None, 2, 0, 1024, 0, None),
+    lambda l: l.kc_allreduce_bf16_nvls(16, 2, 0, 1000, 0, None),           # count % (8 * ranks)
+    lambda l: l.kc_w4a16_tile_weights(None, None, 16, 128, None),
+    lambda l: l.kc_w4a16_tile_weights(16, 16, 16, 100, None),              # K % 128
+    lambda l: l.kc_gemv_w4a16_grouped_tiled(None, None, None, 1, 1, 128, None),
+    lambda l: l.kc_selftest_stream_read(None, 16, 0, None, None),
 ])
 def test_host_validation_rejects_without_launching(call):
     l = kc_lib.lib()

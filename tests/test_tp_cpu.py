@@ -163,3 +163,63 @@ def test_driver_operand_checks():
     tp.check_row_parallel_fp8(M, 32, a, torch.zeros(M), w, torch.zeros(32), cuda=False)
     with pytest.raises(ValueError, match="w_codes_shard"):
         tp.check_row_parallel_fp8(M, 32, a, torch.zeros(M), w[:, :64], torch.zeros(32), cuda=False)
+
+
+def _fused_schedule(R, tiles_m, tiles_n, rank, L):
+    """The tile walk of kc_gemm_fp8_allreduce (gemm_fp8.cu, tile_coords<RS>):
+    linear tile L -> (m_tile, n_tile, owner, index within the owner's block).
+    Output rows are owned in R blocks; rank walks the owners rank+1, ..., rank."""
+    tmo, per = tiles_m // R, (tiles_m // R) * tiles_n
+    b, j = L // per, L % per
+    owner = (rank + 1 + b) % R
+    return owner * tmo + j % tmo, j // tmo, owner, j
+
+
+@pytest.mark.parametrize("R", [2, 4, 8])
+def test_fused_row_parallel_schedule(R):
+    """The epilogue-fused row-parallel sum, restated on the host with numpy:
+    every rank visits every tile once; every (owner, source) partial has its
+    own receive slot (rank - owner - 1) mod R; a source reaches each tile of
+    an owner's block before the owner does (the owner's block comes last in
+    its own walk, so its flag waits follow the partials); and owner-side
+    sums of bf16-rounded partials into the owner's fp32 tile give the
+    unsharded FP8 GEMM within the bf16 bound."""
+    tiles_m, tiles_n = 2 * R, 3
+    tiles = tiles_m * tiles_n
+    seen = {}
+    for rank in range(R):
+        coords = [_fused_schedule(R, tiles_m, tiles_n, rank, L) for L in range(tiles)]
+        assert len({(m, n) for m, n, _, _ in coords}) == tiles          # every tile once
+        for pos, (m, n, owner, j) in enumerate(coords):
+            seen.setdefault((m, n), {})[rank] = (pos, owner, j)
+    for (m, n), by_rank in seen.items():
+        owners = {o for _, o, _ in by_rank.values()}
+        assert len(owners) == 1
+        owner = owners.pop()
+        own_pos = by_rank[owner][0]
+        slots = {(src - owner - 1) % R for src in by_rank if src != owner}
+        assert slots == set(range(R - 1))                               # one slot per source
+        # the owner handles its block last, so every source's block position is earlier
+        tmo = tiles_m // R
+        assert own_pos // (tmo * tiles_n) == R - 1
+        for src, (pos, _, _) in by_rank.items():
+            if src != owner:
+                assert pos // (tmo * tiles_n) < R - 1
+    # numerics: K split in R shards, bf16 partials summed by the owner in slot order
+    rng = np.random.default_rng(R)
+    Mt, Nt, Kt = 8 * R, 16, 64 * R
+    a = rng.standard_normal((Mt, Kt)).astype(np.float32)
+    w = rng.standard_normal((Nt, Kt)).astype(np.float32)
+    full = a.astype(np.float64) @ w.T.astype(np.float64)
+    parts = [a[:, r * Kt // R:(r + 1) * Kt // R] @ w[:, r * Kt // R:(r + 1) * Kt // R].T for r in range(R)]
+    bf16 = lambda v: O.bf16_bits_to_f32(O.f32_to_bf16_bits(v.astype(np.float32)))   # noqa: E731
+    rows = Mt // R
+    out = np.empty((Mt, Nt), np.float32)
+    for owner in range(R):
+        blk = slice(owner * rows, (owner + 1) * rows)
+        acc = parts[owner][blk].astype(np.float32)
+        for sl in range(R - 1):
+            src = (owner + 1 + sl) % R                                   # slot sl's source
+            acc = acc + bf16(parts[src][blk])
+        out[blk] = bf16(acc)
+    assert np.max(np.abs(out - full)) / np.max(np.abs(full)) <= 1e-2

@@ -260,11 +260,15 @@ class GemvW4A16(Workload):
     kernel = "gemv_w4a16"
     profile = "gemv_w4a16_7b_decode_m1"
 
-    def __init__(self, torch, l, dev, s_ptr, rank, world=1, layers=LAYERS, weights="tiled"):
+    def __init__(self, torch, l, dev, s_ptr, rank, world=1, layers=LAYERS, weights="tiled", M=1):
         super().__init__(torch, l, dev, s_ptr, rank, world)
         import kc_lib
         self.kc_lib = kc_lib
         self.weights = weights
+        self.M = M
+        if M != 1:   # the other batch sizes of the decode configuration
+            self.workload_id = f"7b-decode-linear-set-m{M}"
+            self.metric = f"W4A16 GEMV HBM GB/s (7B decode linear set, M={M})"
         self.n_layers = layers
         self.launches_per_step = layers
         self.layers = []
@@ -273,8 +277,8 @@ class GemvW4A16(Workload):
         # (each problem's slice stays 16-byte aligned: K*2 and N*4 bytes)
         kx = sum(K for _, K, _ in SHAPES)
         ny = sum(N for _, _, N in SHAPES)
-        self.x_all = torch.randn(layers * kx, device=dev, generator=self.gen).bfloat16()
-        self.y_all = torch.empty(layers * ny, dtype=torch.float32, device=dev)
+        self.x_all = torch.randn(layers * kx * M, device=dev, generator=self.gen).bfloat16()
+        self.y_all = torch.empty(layers * ny * M, dtype=torch.float32, device=dev)
         xo = yo = 0
         for _ in range(layers):
             probs = []
@@ -283,10 +287,10 @@ class GemvW4A16(Workload):
                                        generator=self.gen)
                 scales = (torch.rand(N, K // GROUP, device=dev, generator=self.gen) * 0.018
                           + 0.002).half()
-                x = self.x_all[xo:xo + K].view(1, K)
-                y = self.y_all[yo:yo + N].view(1, N)
-                xo += K
-                yo += N
+                x = self.x_all[xo:xo + M * K].view(M, K)
+                y = self.y_all[yo:yo + M * N].view(M, N)
+                xo += M * K
+                yo += M * N
                 probs.append((packed, scales, x, y, N, K))
             tiled = None
             if self.weights == "tiled":
@@ -311,9 +315,9 @@ class GemvW4A16(Workload):
     def _grouped(self, layer, st):
         _, arr, _, tarr = layer
         if tarr is not None:
-            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped_tiled(arr, tarr, None, 4, 1, GROUP, st))
+            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped_tiled(arr, tarr, None, 4, self.M, GROUP, st))
         else:
-            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, 1, GROUP, st))
+            self.kc_lib.check(self.l.kc_gemv_w4a16_grouped(arr, 4, self.M, GROUP, st))
 
     def _launch_all(self):
         # launched on the current stream: the capture stream inside the graph
@@ -352,11 +356,11 @@ class GemvW4A16(Workload):
         self.graph.replay()
 
     def work_per_step(self):
-        return layer_bytes(1) * self.n_layers
+        return layer_bytes(self.M) * self.n_layers
 
     def config(self):
         return {"workload": self.workload_id, "layers": self.n_layers,
-                "shapes_KN": [[K, N] for _, K, N in SHAPES], "M": 1, "group_size": GROUP,
+                "shapes_KN": [[K, N] for _, K, N in SHAPES], "M": self.M, "group_size": GROUP,
                 "weights": ("packed [N, K/2] (the reference layout)" if self.weights == "packed" else
                             "tile-ordered (kc_w4a16_tile_weights, converted once at load)"),
                 "bytes_per_step": self.work_per_step(),
@@ -377,8 +381,8 @@ class GemvW4A16(Workload):
         torch = self.torch
         self.h_x = self.x_all.cpu().pin_memory()
         self.h_y = torch.empty(self.y_all.shape, dtype=self.y_all.dtype).pin_memory()
-        kx = sum(K for _, K, _ in SHAPES)
-        ny = sum(N for _, _, N in SHAPES)
+        kx = sum(K for _, K, _ in SHAPES) * self.M
+        ny = sum(N for _, _, N in SHAPES) * self.M
         per = (self.n_layers + self.E2E_PARTS - 1) // self.E2E_PARTS
         self.parts = []
         for p0 in range(0, self.n_layers, per):
@@ -1151,7 +1155,8 @@ def run_workload(name, args, torch, dist, l, dev, stream, s_ptr, world, rank, lo
     JSON line from rank 0.  Returns the exit status (3: the gate failed)."""
     W = WORKLOADS[name]
     if W is GemvW4A16:
-        wl = W(torch, l, dev, s_ptr, rank, world, layers=args.layers, weights=args.gemv_weights)
+        wl = W(torch, l, dev, s_ptr, rank, world, layers=args.layers, weights=args.gemv_weights,
+               M=args.gemv_m)
         wl.use_graph = not args.no_graph
     else:
         wl = W(torch, l, dev, s_ptr, rank, world)
@@ -1481,6 +1486,9 @@ def main(argv=None) -> int:
     ap.add_argument("--gemv-weights", choices=["packed", "tiled"], default="tiled",
                     help="gemv: weights in the reference's packed [N, K/2] layout or the library's "
                          "tile-ordered layout (kc_w4a16_tile_weights, converted once at load)")
+    ap.add_argument("--gemv-m", type=int, default=1, choices=[1, 4, 16],
+                    help="gemv: activation rows (the decode configuration's batch sizes; the "
+                         "headline is M = 1)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="gemv: decoder layers per step (default 32; fewer only for profiling)")
     ap.add_argument("--heat-s", type=float, default=1.5,
